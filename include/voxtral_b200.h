@@ -1,0 +1,182 @@
+/* voxtral_b200.h — C ABI of the B200-native Voxtral decode path.
+ *
+ * This is the boundary a host binding (Node N-API / FFI, Python ctypes, C, C++)
+ * loads in place of the reference's WebGPU engine internals.  The reference's
+ * public TypeScript class VoxtralEngine (svenflow/webgpu-voxtral, src/engine.ts:291)
+ * keeps its signatures; its methods call these functions.  Each declaration cites
+ * the reference interface it replaces (file:line in the reference tree).
+ *
+ * Conventions (mirroring src/engine.ts):
+ *  - Ownership: the library owns all device memory.  Caller arrays are copied in
+ *    during the call; output arrays are caller-allocated host memory filled before
+ *    the call returns (src/engine.ts:2436-2451 copies caller arrays likewise).
+ *  - Errors: every int-returning function returns VX_OK (0) or a negative VX_E_*
+ *    code, and vx_last_error() describes the last failure of that handle (the
+ *    reference throws `new Error(...)`, e.g. src/engine.ts:314-320, 666, 2425).
+ *    No C++ exception crosses this boundary.
+ *  - Threading: one handle per host thread; calls on one handle are serialised by
+ *    the caller (the reference engine is single-threaded, src/engine.ts:299).
+ *  - Values: weights are IEEE binary16 bit patterns, activations f32, token ids
+ *    int32, codes uint32 (semantic 0..8193, acoustic 2..22).
+ */
+#ifndef VOXTRAL_B200_H
+#define VOXTRAL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VX_OK 0
+#define VX_E_INVALID (-1) /* bad argument (null pointer, size, name)           */
+#define VX_E_CUDA (-2)    /* a CUDA runtime / driver call failed                 */
+#define VX_E_STATE (-3)   /* not ready: weights not loaded, slot not prefilled   */
+#define VX_E_RANGE (-4)   /* token / code / position / slot out of range         */
+#define VX_E_NOMEM (-5)   /* device allocation failed                            */
+#define VX_E_NCCL (-6)    /* NCCL missing or a collective failed                 */
+#define VX_E_DEVICE (-7)  /* a kernel reported a device-side error (bounded wait
+                             expired, index out of range); the handle stays usable */
+
+typedef struct vx_handle vx_handle;
+
+/* VoxtralConfig (src/types.ts:10-37, defaultConfig :70-97) + EngineOptions
+ * (src/engine.ts:213-219) + the B200 engine's own options. */
+typedef struct vx_config {
+  /* backbone (BackboneConfig) */
+  int32_t dim, n_layers, head_dim, hidden_dim, n_heads, n_kv_heads, vocab_size;
+  float rope_theta, norm_eps;
+  /* acoustic (flow-matching) transformer (FMTransformerConfig) */
+  int32_t fm_n_layers, fm_nfe;
+  float fm_cfg_alpha;
+  int32_t fm_n_acoustic, fm_semantic_vocab, acoustic_levels;
+  int32_t audio_vocab; /* rows of audio_codebook_embeddings (9088) */
+  /* engine */
+  int32_t max_seq_len; /* EngineOptions.maxSeqLen (default 4096) */
+  int32_t max_slots;   /* utterance slots that can decode concurrently */
+  int32_t max_frames;  /* capacity of each slot's on-device code ring */
+  int32_t max_voice_rows;
+  int32_t enable_fm;   /* allocate the acoustic transformer */
+  int32_t device;      /* CUDA device ordinal */
+  int32_t tp_size, tp_rank; /* tensor parallelism (1 = off) */
+} vx_config;
+
+/* defaultConfig (src/types.ts:70-122) with maxSeqLen 4096, 1 slot. */
+void vx_default_config(vx_config* cfg);
+
+/* new VoxtralEngine(options) + init() (src/engine.ts:301-344): selects the
+ * device, allocates weights, KV cache and work buffers. */
+int vx_create(const vx_config* cfg, vx_handle** out);
+
+/* destroy() (src/engine.ts:2621-2633). */
+void vx_destroy(vx_handle* h);
+
+/* Message of the last failure on this handle ("" if none). */
+const char* vx_last_error(const vx_handle* h);
+
+/* Replaces loadWeights()/loadWeightsFromHF() (src/engine.ts:539-586) for the
+ * benchmark: fills every tensor with the synthetic values of vx_rng.h
+ * (matrices N(0,0.02) in f16 from stream fnv1a(name) of `seed`, norm gains 1). */
+int vx_init_random_weights(vx_handle* h, uint64_t seed);
+
+/* One tensor of organizeWeights (src/engine.ts:659-743) by its checkpoint name
+ * (e.g. "layers.3.attention.wk.weight"), row-major f16 bits, full (unsharded)
+ * shape; the library keeps the shard of its tp_rank.  Returns VX_E_INVALID for an
+ * unknown name or a wrong element count. */
+int vx_load_tensor(vx_handle* h, const char* name, const uint16_t* f16, size_t n_elems);
+
+/* Completion of loadWeights() after the vx_load_tensor calls: builds the derived
+ * frame-independent tables (time_projection of the 7 Euler times). */
+int vx_mark_weights_loaded(vx_handle* h);
+
+/* Element count of a named tensor (0 if unknown). */
+size_t vx_tensor_numel(const vx_handle* h, const char* name);
+
+/* Copy a named tensor back (f16 bits) — used to verify loaded/synthetic weights. */
+int vx_read_tensor(vx_handle* h, const char* name, uint16_t* out, size_t n_elems);
+
+/* reset() (src/engine.ts:2323-2327): position 0, frame 0 for one slot. */
+int vx_reset(vx_handle* h, int32_t slot);
+
+int vx_get_position(vx_handle* h, int32_t slot, int32_t* pos);
+
+/* Token-by-token prefill of generate() (src/engine.ts:2457-2472): prompt
+ * positions [audio_start, audio_start+audio_count) take the rows of `voice`
+ * ([audio_count][dim] f32, REPLACING the token embedding, :843-854); every other
+ * position embeds tokens[i].  Starts at the slot's current position. */
+int vx_prefill(vx_handle* h, int32_t slot, const int32_t* tokens, int32_t n_tokens, int32_t audio_start,
+               int32_t audio_count, const float* voice);
+
+/* backboneStep (src/engine.ts:814-1042) as exposed by backboneStepAndRead /
+ * debugBackboneStepFull (:2333-2358): one token through the backbone at the
+ * slot's position; embed = tok_embeddings[token] (or audio_embeddings[token] if
+ * use_audio_embedding), or the caller's row `embed` [dim] if non-null.
+ * normed_out [dim] (nullable) receives the final-norm output that feeds the FM.
+ * argmax_out (nullable) runs the tied LM head + argmax (:1017-1041). */
+int vx_backbone_step(vx_handle* h, int32_t slot, int32_t token, int32_t use_audio_embedding, const float* embed,
+                     float* normed_out, int32_t* argmax_out);
+
+/* The frame-loop backbone step of generate() (src/engine.ts:2499-2541): the
+ * input is multiCodebookEmbed(semantic, acoustic[36]) (src/shaders.ts:1878-1917). */
+int vx_backbone_step_codes(vx_handle* h, int32_t slot, uint32_t semantic_code, const uint32_t* acoustic_codes,
+                           float* normed_out);
+
+/* fmForward (src/engine.ts:1240-1380) on the slot's current normed state, as
+ * exposed by debugFMStep(noise) / fmStepAndRead (:2363-2398).  noise [36]
+ * (nullable: the slot's seeded stream).  Outputs (all nullable): semantic logits
+ * [semantic_vocab], the masked-argmax semantic code (index 0 and >= 8194 masked,
+ * :2559-2563), acoustic codes [36], x_final [36]. */
+int vx_fm_step(vx_handle* h, int32_t slot, const float* noise, float* semantic_logits, uint32_t* semantic_code,
+               uint32_t* acoustic_codes, float* x_final);
+
+/* debugBackboneLayerByLayer (src/engine.ts:2106-2287) at the slot's position for
+ * tok_embeddings[token]: out [(4*n_layers+3)][dim] = embed, per layer {attn_norm,
+ * attn_out (hidden after the attention residual), ffn_norm, ffn_out}, final_norm,
+ * hidden.  Advances the position like the reference. */
+int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out);
+
+/* Device-resident frame loop of generate() (src/engine.ts:2498-2585) with the
+ * host round trips removed: n_frames frames starting at the slot's current frame,
+ * each one CUDA graph.  with_fm = 1: frame f > 0 embeds frame f-1's codes, runs the
+ * backbone, then fmForward with the slot's noise stream and masked argmax (frame
+ * 0 runs the FM on the state left by the AUDIO kick).  with_fm = 0 (backbone-only):
+ * frame 0 is the AUDIO kick (token 24, text embedding, :2481-2487) and frame f > 0
+ * embeds the synthetic codes of frame f-1.  Asynchronous: returns after enqueueing;
+ * read results with vx_read_codes / vx_read_normed after vx_synchronize. */
+int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm);
+
+/* Seeds of the slot's synthetic streams (FM noise, backbone-only feedback codes);
+ * `utt` selects the utterance stream of vx_rng.h. */
+int vx_set_streams(vx_handle* h, int32_t slot, uint64_t noise_seed, uint64_t codes_seed, int32_t utt);
+
+/* Codes of frames [frame0, frame0+n): out [n][37] = semantic, 36 acoustic. */
+int vx_read_codes(vx_handle* h, int32_t slot, int32_t frame0, int32_t n, uint32_t* out);
+/* Final-norm state of frames [frame0, frame0+n): out [n][dim]. */
+int vx_read_normed(vx_handle* h, int32_t slot, int32_t frame0, int32_t n, float* out);
+
+/* Save / restore a slot's decode state (position, frame, codes, normed state):
+ * a checkpoint taken after prefill lets a benchmark replay the same decode. */
+int vx_checkpoint(vx_handle* h, int32_t slot);
+int vx_rewind(vx_handle* h, int32_t slot);
+
+/* Use the caller's CUDA stream (cudaStream_t as void*, e.g. torch's current
+ * stream) for all later work; NULL restores the handle's own stream. */
+int vx_set_stream(vx_handle* h, void* stream);
+int vx_synchronize(vx_handle* h);
+
+/* Kernel launches enqueued by this handle since creation (graph launches count
+ * the kernels they contain). */
+int64_t vx_launch_count(const vx_handle* h);
+
+/* Tensor parallelism over NCCL (batch-1 latency, heads and FFN columns
+ * sharded): the unique id comes from vx_nccl_unique_id on rank 0 and is shared by
+ * the host (e.g. torch.distributed).  nccl_lib: path of libnccl.so.2 (NULL: the
+ * default search path). */
+int vx_nccl_unique_id(const char* nccl_lib, uint8_t out[128]);
+int vx_tp_init(vx_handle* h, const char* nccl_lib, const uint8_t id[128]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VOXTRAL_B200_H */

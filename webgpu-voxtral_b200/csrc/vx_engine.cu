@@ -1,0 +1,1150 @@
+// vx_engine.cu — the B200 decode engine behind include/voxtral_b200.h.
+//
+// Replaces the WebGPU orchestration of the reference's VoxtralEngine
+// (src/engine.ts: createWorkBuffers :453-508, createKVCaches :510-530,
+// organizeWeights :659-743, backboneStep :814-1042, fmTransformerPass :1057-1225,
+// fmForward :1240-1380, generate :2416-2616).
+//
+// Memory (HBM): one arena holds all weights in streaming order per layer
+//   [wq;wk;wv] [6144,3072] | wo [3072,4096] | [w1;w3] [18432,3072] | w2 [3072,9216] | norms
+// so that every projection is one contiguous weight stream; a paged f16 KV pool
+// (pages of 64 positions, page table per slot); f32 activations per slot.
+// Each backbone step / FM pass / decode frame is one CUDA graph whose kernels
+// read the slot's position and inputs from device memory (SlotState), so one
+// captured graph serves every step.  Kernels are chained with programmatic
+// dependent launch.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/voxtral_b200.h"
+#include "k_attn.cuh"
+#include "k_gemv.cuh"
+#include "k_misc.cuh"
+
+using namespace vx;
+
+namespace {
+
+constexpr int kPage = 64;
+constexpr int kAudioKick = 24;   // AUDIO token fed through the text embedding after prefill
+
+struct LayerW {
+  __half *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr, *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+// One checkpoint tensor and where its (shard of) values live on the device.
+struct TensorSlot {
+  __half* dst;
+  long long ld;               // destination row stride (elements)
+  long long rows, cols;       // local block
+  long long full_rows, full_cols;
+  long long row0, col0;       // block origin inside the full tensor
+  bool is_norm;
+};
+
+struct NcclApi {
+  void* lib = nullptr;
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  const char* (*getErrorString)(ncclResult_t) = nullptr;
+  bool load(const char* path, std::string& err) {
+    if (lib) return true;
+    lib = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!lib) { err = std::string("cannot load NCCL: ") + dlerror(); return false; }
+    getUniqueId = (decltype(getUniqueId))dlsym(lib, "ncclGetUniqueId");
+    commInitRank = (decltype(commInitRank))dlsym(lib, "ncclCommInitRank");
+    allReduce = (decltype(allReduce))dlsym(lib, "ncclAllReduce");
+    commDestroy = (decltype(commDestroy))dlsym(lib, "ncclCommDestroy");
+    getErrorString = (decltype(getErrorString))dlsym(lib, "ncclGetErrorString");
+    if (!getUniqueId || !commInitRank || !allReduce || !commDestroy) { err = "NCCL symbols missing"; return false; }
+    return true;
+  }
+};
+NcclApi g_nccl;
+
+}  // namespace
+
+struct vx_handle {
+  vx_config cfg{};
+  int dev = 0, num_sms = 148;
+  cudaStream_t own_stream = nullptr, stream = nullptr;
+  bool use_pdl = true;
+  std::string err;
+  long long launches = 0;
+
+  // dims (local to this TP rank where sharded)
+  int D = 0, L = 0, HD = 128, F = 0, FL = 0, NH = 0, NKV = 0, QD = 0, KVD = 0, QKVD = 0;
+  int V = 0, AV = 0, NAC = 36, SEMV = 0, Fl = 0;   // Fl: local FFN width
+  int tp = 1, rank = 0;
+
+  // weights
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<LayerW> layers, fm_layers;
+  __half *tok_emb = nullptr, *audio_emb = nullptr, *final_norm = nullptr;
+  __half *fm_in = nullptr, *fm_head = nullptr, *fm_time = nullptr, *fm_norm = nullptr, *fm_ac = nullptr;
+  std::unordered_map<std::string, TensorSlot> tensors;
+  bool weights_ready = false, tp_table_ready = false;
+
+  // KV cache
+  __half* kv_pool = nullptr;
+  long long kv_rows = 0;
+  int max_pages = 0, n_splits = 1;
+  int32_t* page_table = nullptr;
+  CUtensorMap kv_map;
+  float* attn_part = nullptr;
+  int* attn_tickets = nullptr;
+  float* rope_freq = nullptr;
+
+  // slots and activations
+  int B = 1;
+  SlotState* slots = nullptr;
+  float *h = nullptr, *q = nullptr, *att = nullptr, *g = nullptr, *normed = nullptr, *rows_in = nullptr;
+  int32_t* prompt = nullptr;
+  float* voice = nullptr;
+  uint32_t* code_ring = nullptr;
+  float* normed_ring = nullptr;
+  float* logits = nullptr;
+  int32_t* argmax_dev = nullptr;
+  float* dbg = nullptr;
+  // FM work buffers (per slot)
+  float *fm_head_out = nullptr, *fm_seq = nullptr, *fm_qkv = nullptr, *fm_att = nullptr, *fm_g = nullptr;
+  float *fm_vel = nullptr, *fm_x = nullptr, *fm_noise = nullptr, *fm_xfinal = nullptr, *tp_table = nullptr,
+        *te_tmp = nullptr;
+  // checkpoint copies
+  SlotState* ck_slots = nullptr;
+  float* ck_normed = nullptr;
+  std::vector<int> ck_pos_host, ck_frame_host;
+
+  std::vector<int> pos_host, frame_host, prompt_len_host;
+
+  // graphs: per slot
+  struct G {
+    cudaGraphExec_t exec = nullptr;
+    long long kernels = 0;
+  };
+  std::vector<G> g_step, g_fm, g_frame_fm, g_frame_bb;
+
+  // staging
+  uint8_t* pinned = nullptr;
+  size_t pinned_bytes = 0;
+
+  // TP
+  ncclComm_t comm = nullptr;
+
+  int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    err = buf;
+    return code;
+  }
+};
+
+#define CK(...)                                                                                 \
+  do {                                                                                          \
+    cudaError_t e_ = (__VA_ARGS__);                                                                  \
+    if (e_ != cudaSuccess) return h->fail(VX_E_CUDA, "%s: %s", #__VA_ARGS__, cudaGetErrorString(e_)); \
+  } while (0)
+
+namespace {
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(vx_handle* h, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = h->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = h->use_pdl ? 1 : 0;
+  h->launches++;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+template <int M, int R, int CPL, int EPI, bool NORM>
+cudaError_t gemv_attr() {
+  return cudaFuncSetAttribute(gemv::k_gemv<M, R, CPL, EPI, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)gemv::kSmemBytes);
+}
+
+// Every GEMV instantiation the programs use gets its shared-memory opt-in at
+// engine creation, before any stream capture.
+int prime_kernel_attrs(vx_handle* h) {
+  using namespace gemv;
+  CK(gemv_attr<1, 6, 3, kQkv, true>());
+  CK(gemv_attr<1, 4, 4, kResid, false>()); CK(gemv_attr<1, 4, 4, kStore, false>());
+  CK(gemv_attr<1, 8, 2, kResid, false>()); CK(gemv_attr<1, 8, 2, kStore, false>());
+  CK(gemv_attr<1, 8, 1, kResid, false>()); CK(gemv_attr<1, 8, 1, kStore, false>());
+  CK(gemv_attr<1, 6, 3, kSwiglu, true>());
+  CK(gemv_attr<1, 2, 9, kResid, false>()); CK(gemv_attr<1, 2, 9, kStore, false>());
+  CK(gemv_attr<1, 2, 5, kResid, false>()); CK(gemv_attr<1, 2, 5, kStore, false>());
+  CK(gemv_attr<1, 6, 3, kResid, false>()); CK(gemv_attr<1, 6, 3, kStore, false>());
+  CK(gemv_attr<6, 4, 3, kStore, true>()); CK(gemv_attr<6, 4, 4, kResid, false>());
+  CK(gemv_attr<6, 4, 3, kSwiglu, true>()); CK(gemv_attr<6, 4, 3, kResid, false>());
+  CK(gemv_attr<2, 6, 3, kStore, true>());
+  CK(cudaFuncSetAttribute(attn::k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn::kSmemBytes));
+  return VX_OK;
+}
+
+template <int M, int R, int CPL, int EPI, bool NORM>
+int run_gemv(vx_handle* h, const gemv::Params& p) {
+  auto kern = gemv::k_gemv<M, R, CPL, EPI, NORM>;
+  constexpr int ORT = EPI == gemv::kSwiglu ? R / 2 : R;
+  if (p.kc % 128 || (p.kc / 128 + gemv::kCW - 1) / gemv::kCW != CPL || (long long)R * p.kc * 2 > gemv::kStageBytes ||
+      p.col0 % 128 ||
+      p.col0 + p.kc > p.ldw || p.rows <= 0)
+    return h->fail(VX_E_INVALID, "gemv shape: rows %d kc %d col0 %d ldw %lld (CPL %d R %d)", p.rows, p.kc, p.col0,
+                   p.ldw, CPL, R);
+  const int ntiles = (p.rows + ORT - 1) / ORT;
+  const int grid = std::min(ntiles, h->num_sms);
+  CK(launch(h, kern, dim3(grid), dim3(gemv::kThreads), gemv::kSmemBytes, p));
+  return VX_OK;
+}
+
+void* carve(uint8_t*& cur, size_t bytes) {
+  void* p = cur;
+  cur += (bytes + 255) & ~size_t(255);
+  return p;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int make_kv_map(vx_handle* h) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (!fn || q != cudaDriverEntryPointSuccess) return h->fail(VX_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {128, (cuuint64_t)h->kv_rows};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = ((EncodeTiledFn)fn)(&h->kv_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, h->kv_pool, dims, strides, box, es,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return h->fail(VX_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VX_OK;
+}
+
+// -------------------------------------------------------------------- programs
+int check_device_error(vx_handle* h) {
+  int e = 0;
+  CK(cudaMemcpyFromSymbol(&e, vx::vx_dev_error, sizeof(int)));
+  if (e) {
+    int z = 0;
+    cudaMemcpyToSymbol(vx::vx_dev_error, &z, sizeof(int));
+    static const char* names[] = {"ok", "TMA stage wait expired", "free-stage wait expired",
+                                  "reduction slot wait expired", "drain wait expired", "index out of range"};
+    return h->fail(VX_E_DEVICE, "device-side error: %s", (e > 0 && e < 6) ? names[e] : "unknown");
+  }
+  return VX_OK;
+}
+
+int allreduce_inplace(vx_handle* h, float* buf, size_t n) {
+  if (h->tp == 1) return VX_OK;
+  ncclResult_t r = g_nccl.allReduce(buf, buf, n, ncclFloat32, ncclSum, h->comm, h->stream);
+  if (r != ncclSuccess)
+    return h->fail(VX_E_NCCL, "ncclAllReduce: %s", g_nccl.getErrorString ? g_nccl.getErrorString(r) : "error");
+  return VX_OK;
+}
+
+struct DebugSink {
+  float* base = nullptr;   // [(4L+3)][D] on device
+};
+
+int dbg_rows(vx_handle* h, const float* src, const __half* w, float* dst) {
+  CK(launch(h, k_rows_copy_or_norm, dim3(1), dim3(256), 0, src, w, dst, h->D, h->cfg.norm_eps));
+  return VX_OK;
+}
+
+// backboneStep for one slot: embed -> L x (norm+QKV+RoPE+KV append, attention,
+// o_proj+residual, norm+gate/up+SwiGLU, down+residual) -> final norm.
+int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const DebugSink* dbg) {
+  const int D = h->D;
+  int rc;
+  EmbedParams ep{};
+  ep.tok = h->tok_emb; ep.vocab = h->V; ep.audio = h->audio_emb; ep.audio_rows = h->AV;
+  ep.slots = h->slots; ep.rows = h->rows_in; ep.prompt = h->prompt; ep.voice = h->voice;
+  ep.max_seq = h->cfg.max_seq_len; ep.max_voice = h->cfg.max_voice_rows; ep.code_ring = h->code_ring;
+  ep.h = h->h + (long long)slot * D; ep.D = D; ep.slot0 = slot;
+  CK(launch(h, k_embed, dim3(1), dim3(256), 0, ep));
+  if (dbg && (rc = dbg_rows(h, ep.h, nullptr, dbg->base))) return rc;
+
+  float* hs = h->h + (long long)slot * D;
+  float* qs = h->q + (long long)slot * h->QD;
+  float* as = h->att + (long long)slot * h->QD;
+  float* gs = h->g + (long long)slot * h->Fl;
+  gemv::KvGeom kg{h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV, kPage};
+  for (int l = 0; l < h->L; ++l) {
+    const LayerW& W = h->layers[l];
+    if (dbg && (rc = dbg_rows(h, hs, W.attn_norm, dbg->base + (size_t)(1 + 4 * l) * D))) return rc;
+    {  // RMSNorm + [wq;wk;wv] + RoPE + q store + K/V append
+      gemv::Params p{};
+      p.W = W.wqkv; p.ldw = D; p.rows = h->QKVD; p.col0 = 0; p.kc = D;
+      p.x = hs; p.ldx = D; p.norm_w = W.attn_norm; p.eps = h->cfg.norm_eps; p.norm_dim = D;
+      p.qkv.q = qs; p.qkv.ldq = h->QD; p.qkv.q_dim = h->QD; p.qkv.kv_dim = h->KVD; p.qkv.kv = kg; p.qkv.layer = l;
+      p.qkv.pos = &h->slots[0].pos; p.qkv.pos_stride = kPosStride; p.qkv.slot0 = slot; p.qkv.rope_freq = h->rope_freq;
+      if ((rc = run_gemv<1, 6, 3, gemv::kQkv, true>(h, p))) return rc;
+    }
+    {  // split-KV flash-decode
+      attn::Params ap{};
+      ap.q = qs; ap.ldq = h->QD; ap.out = as; ap.ldo = h->QD;
+      ap.part = h->attn_part + (long long)slot * h->NKV * h->n_splits * attn::kGqa * attn::kPartStride;
+      ap.tickets = h->attn_tickets + (long long)slot * h->NKV;
+      ap.kv = kg; ap.layer = l; ap.pos = &h->slots[0].pos; ap.pos_stride = kPosStride; ap.slot0 = slot;
+      ap.n_splits = h->n_splits; ap.scale = 1.0f / sqrtf((float)h->HD);
+      CK(launch(h, attn::k_attn_decode, dim3(h->NKV, h->n_splits, 1), dim3(attn::kThreads), attn::kSmemBytes,
+                h->kv_map, ap));
+    }
+    {  // o_proj + residual (TP: rank-local partial, then allreduce of h)
+      gemv::Params p{};
+      p.W = W.wo; p.ldw = h->QD; p.rows = D; p.col0 = 0; p.kc = h->QD; p.x = as; p.ldx = h->QD; p.y = hs; p.ldy = D;
+      if (h->QD == 4096) rc = (h->rank == 0) ? run_gemv<1, 4, 4, gemv::kResid, false>(h, p) : run_gemv<1, 4, 4, gemv::kStore, false>(h, p);
+      else if (h->QD == 2048) rc = (h->rank == 0) ? run_gemv<1, 8, 2, gemv::kResid, false>(h, p) : run_gemv<1, 8, 2, gemv::kStore, false>(h, p);
+      else if (h->QD == 1024) rc = (h->rank == 0) ? run_gemv<1, 8, 1, gemv::kResid, false>(h, p) : run_gemv<1, 8, 1, gemv::kStore, false>(h, p);
+      else if (h->QD == 512) rc = (h->rank == 0) ? run_gemv<1, 8, 1, gemv::kResid, false>(h, p) : run_gemv<1, 8, 1, gemv::kStore, false>(h, p);
+      else rc = h->fail(VX_E_INVALID, "unsupported local q width %d", h->QD);
+      if (rc) return rc;
+      if ((rc = allreduce_inplace(h, hs, D))) return rc;
+    }
+    if (dbg && (rc = dbg_rows(h, hs, nullptr, dbg->base + (size_t)(2 + 4 * l) * D))) return rc;
+    if (dbg && (rc = dbg_rows(h, hs, W.ffn_norm, dbg->base + (size_t)(3 + 4 * l) * D))) return rc;
+    {  // RMSNorm + [w1;w3] + SwiGLU
+      gemv::Params p{};
+      p.W = W.w13; p.ldw = D; p.second_off = (long long)h->Fl * D; p.rows = h->Fl; p.col0 = 0; p.kc = D;
+      p.x = hs; p.ldx = D; p.norm_w = W.ffn_norm; p.eps = h->cfg.norm_eps; p.norm_dim = D; p.y = gs; p.ldy = h->Fl;
+      if ((rc = run_gemv<1, 6, 3, gemv::kSwiglu, true>(h, p))) return rc;
+    }
+    {  // down + residual
+      gemv::Params p{};
+      p.W = W.w2; p.ldw = h->Fl; p.rows = D; p.col0 = 0; p.kc = h->Fl; p.x = gs; p.ldx = h->Fl; p.y = hs; p.ldy = D;
+      if (h->Fl == 9216) rc = (h->rank == 0) ? run_gemv<1, 2, 9, gemv::kResid, false>(h, p) : run_gemv<1, 2, 9, gemv::kStore, false>(h, p);
+      else if (h->Fl == 4608) rc = (h->rank == 0) ? run_gemv<1, 2, 5, gemv::kResid, false>(h, p) : run_gemv<1, 2, 5, gemv::kStore, false>(h, p);
+      else if (h->Fl == 2304) rc = (h->rank == 0) ? run_gemv<1, 6, 3, gemv::kResid, false>(h, p) : run_gemv<1, 6, 3, gemv::kStore, false>(h, p);
+      else if (h->Fl == 1152) rc = (h->rank == 0) ? run_gemv<1, 8, 2, gemv::kResid, false>(h, p) : run_gemv<1, 8, 2, gemv::kStore, false>(h, p);
+      else rc = h->fail(VX_E_INVALID, "unsupported local FFN width %d", h->Fl);
+      if (rc) return rc;
+      if ((rc = allreduce_inplace(h, hs, D))) return rc;
+    }
+    if (dbg && (rc = dbg_rows(h, hs, nullptr, dbg->base + (size_t)(4 + 4 * l) * D))) return rc;
+  }
+  FinalNormParams fp{};
+  fp.h = hs; fp.w = h->final_norm; fp.out = h->normed + (long long)slot * D; fp.D = D; fp.eps = h->cfg.norm_eps;
+  fp.slots = h->slots; fp.slot0 = slot; fp.inc_pos = 1; fp.inc_frame = inc_frame ? 1 : 0;
+  fp.normed_ring = record ? h->normed_ring : nullptr;
+  CK(launch(h, k_final_norm, dim3(1), dim3(256), 0, fp));
+  if (dbg) {
+    if ((rc = dbg_rows(h, fp.out, nullptr, dbg->base + (size_t)(1 + 4 * h->L) * D))) return rc;
+    if ((rc = dbg_rows(h, hs, nullptr, dbg->base + (size_t)(2 + 4 * h->L) * D))) return rc;
+  }
+  return VX_OK;
+}
+
+FmParams fm_params(vx_handle* h, int slot) {
+  FmParams f{};
+  const int D = h->D;
+  f.slots = h->slots; f.slot = slot;
+  f.head_out = h->fm_head_out + (long long)slot * (h->SEMV + D);
+  f.sem_vocab = h->SEMV; f.D = D;
+  f.host_noise = h->fm_noise + (long long)slot * 36;
+  f.x = h->fm_x + (long long)slot * 36;
+  f.w_in = h->fm_in; f.tp = h->tp_table;
+  f.seq = h->fm_seq + (long long)slot * 6 * D;
+  f.qkv = h->fm_qkv + (long long)slot * 6 * (4096 + 2048);
+  f.att = h->fm_att + (long long)slot * 6 * 4096;
+  f.q_dim = 4096; f.kv_dim = 1024; f.n_heads = 32; f.n_kv = 8;
+  f.vel = h->fm_vel + (long long)slot * 72;
+  f.alpha = h->cfg.fm_cfg_alpha; f.dt = (float)(1.0 / (h->cfg.fm_nfe - 1));
+  f.code_ring = h->code_ring;
+  f.x_final = h->fm_xfinal + (long long)slot * 36;
+  return f;
+}
+
+// fmForward for one slot on its normed state (the FM is not sharded under TP:
+// every rank computes it redundantly).
+int enqueue_fm(vx_handle* h, int slot) {
+  const int D = h->D, F = h->cfg.hidden_dim;
+  int rc;
+  {  // semantic head + llm projection in one weight stream ([8320 + 3072] rows)
+    gemv::Params p{};
+    p.W = h->fm_head; p.ldw = D; p.rows = h->SEMV + D; p.col0 = 0; p.kc = D;
+    p.x = h->normed + (long long)slot * D; p.ldx = D; p.y = h->fm_head_out + (long long)slot * (h->SEMV + D); p.ldy = 0;
+    if ((rc = run_gemv<1, 6, 3, gemv::kStore, false>(h, p))) return rc;
+  }
+  FmParams f = fm_params(h, slot);
+  CK(launch(h, k_fm_prepare, dim3(1), dim3(1024), 0, f));
+  const int steps = h->cfg.fm_nfe - 1;
+  for (int s = 0; s < steps; ++s) {
+    f.step = s;
+    CK(launch(h, k_fm_assemble, dim3((D + 255) / 256), dim3(256), 0, f));
+    for (int l = 0; l < h->cfg.fm_n_layers; ++l) {
+      const LayerW& W = h->fm_layers[l];
+      {
+        gemv::Params p{};
+        p.W = W.wqkv; p.ldw = D; p.rows = 6144; p.col0 = 0; p.kc = D; p.x = f.seq; p.ldx = D;
+        p.norm_w = W.attn_norm; p.eps = 1e-5f; p.norm_dim = D; p.y = const_cast<float*>(f.qkv); p.ldy = 6144;
+        if ((rc = run_gemv<6, 4, 3, gemv::kStore, true>(h, p))) return rc;
+      }
+      CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, f));
+      {
+        gemv::Params p{};
+        p.W = W.wo; p.ldw = 4096; p.rows = D; p.col0 = 0; p.kc = 4096; p.x = f.att; p.ldx = 4096; p.y = f.seq; p.ldy = D;
+        if ((rc = run_gemv<6, 4, 4, gemv::kResid, false>(h, p))) return rc;
+      }
+      {
+        gemv::Params p{};
+        p.W = W.w13; p.ldw = D; p.second_off = (long long)F * D; p.rows = F; p.col0 = 0; p.kc = D;
+        p.x = f.seq; p.ldx = D; p.norm_w = W.ffn_norm; p.eps = 1e-5f; p.norm_dim = D;
+        p.y = h->fm_g + (long long)slot * 6 * F; p.ldy = F;
+        if ((rc = run_gemv<6, 4, 3, gemv::kSwiglu, true>(h, p))) return rc;
+      }
+      for (int c = 0; c < F / 3072; ++c) {
+        gemv::Params p{};
+        p.W = W.w2; p.ldw = F; p.rows = D; p.col0 = c * 3072; p.kc = 3072;
+        p.x = h->fm_g + (long long)slot * 6 * F; p.ldx = F; p.y = f.seq; p.ldy = D;
+        if ((rc = run_gemv<6, 4, 3, gemv::kResid, false>(h, p))) return rc;
+      }
+    }
+    {  // final norm of position 0 of both sequences + acoustic_codebook_output
+      gemv::Params p{};
+      p.W = h->fm_ac; p.ldw = D; p.rows = 36; p.col0 = 0; p.kc = D; p.x = f.seq; p.ldx = 3LL * D;
+      p.norm_w = h->fm_norm; p.eps = 1e-5f; p.norm_dim = D; p.y = const_cast<float*>(f.vel); p.ldy = 36;
+      if ((rc = run_gemv<2, 6, 3, gemv::kStore, true>(h, p))) return rc;
+    }
+    CK(launch(h, k_fm_euler, dim3(1), dim3(64), 0, f, (int)(s == steps - 1)));
+  }
+  return VX_OK;
+}
+
+// time_projection(time_embedding(t_s)) for the 7 Euler times: frame-independent,
+// so computed once instead of once per step of every frame.
+int build_tp_table(vx_handle* h) {
+  const int D = h->D, steps = h->cfg.fm_nfe - 1;
+  for (int s = 0; s < steps; ++s) {
+    const float t = (float)((double)s / steps);
+    k_time_embed<<<(D / 2 + 255) / 256, 256, 0, h->stream>>>(t, D, h->te_tmp);
+    h->launches++;
+    CK(cudaGetLastError());
+    gemv::Params p{};
+    p.W = h->fm_time; p.ldw = D; p.rows = D; p.col0 = 0; p.kc = D; p.x = h->te_tmp; p.ldx = D;
+    p.y = h->tp_table + (long long)s * D; p.ldy = D;
+    int rc = run_gemv<1, 6, 3, gemv::kStore, false>(h, p);
+    if (rc) return rc;
+  }
+  CK(cudaStreamSynchronize(h->stream));
+  h->tp_table_ready = true;
+  return VX_OK;
+}
+
+enum Prog { kProgStep = 0, kProgFm = 1, kProgFrameFm = 2, kProgFrameBb = 3 };
+
+int enqueue_prog(vx_handle* h, int prog, int slot) {
+  int rc;
+  switch (prog) {
+    case kProgStep: return enqueue_backbone(h, slot, false, false, nullptr);
+    case kProgFm: return enqueue_fm(h, slot);
+    case kProgFrameFm: {
+      // frame f > 0: multiCodebookEmbed(frame f-1 codes) -> backbone -> FM
+      if ((rc = enqueue_backbone(h, slot, false, true, nullptr))) return rc;
+      return enqueue_fm(h, slot);
+    }
+    case kProgFrameBb: return enqueue_backbone(h, slot, true, true, nullptr);
+  }
+  return h->fail(VX_E_INVALID, "bad program");
+}
+
+int run_prog(vx_handle* h, int prog, int slot) {
+  std::vector<vx_handle::G>* tab = prog == kProgStep ? &h->g_step : prog == kProgFm ? &h->g_fm
+                                 : prog == kProgFrameFm ? &h->g_frame_fm : &h->g_frame_bb;
+  vx_handle::G& g = (*tab)[slot];
+  if (!g.exec) {
+    cudaGraph_t graph;
+    const long long before = h->launches;
+    CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_prog(h, prog, slot);
+    cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+    if (rc) { if (ce == cudaSuccess) cudaGraphDestroy(graph); return rc; }
+    if (ce != cudaSuccess) return h->fail(VX_E_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+    cudaError_t ie = cudaGraphInstantiate(&g.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return h->fail(VX_E_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
+    g.kernels = h->launches - before;
+    h->launches = before;
+  }
+  CK(cudaGraphLaunch(g.exec, h->stream));
+  h->launches += g.kernels;
+  return VX_OK;
+}
+
+int check_slot(vx_handle* h, int slot) {
+  if (!h) return VX_E_INVALID;
+  if (slot < 0 || slot >= h->B) return h->fail(VX_E_RANGE, "slot %d out of range [0,%d)", slot, h->B);
+  if (!h->weights_ready) return h->fail(VX_E_STATE, "Engine not initialized. Call init() and loadWeights() first.");
+  return VX_OK;
+}
+
+int slot_update(vx_handle* h, int slot, const SlotUpdate& u) {
+  k_slot_update<<<1, 32, 0, h->stream>>>(h->slots, slot, u);
+  h->launches++;
+  CK(cudaGetLastError());
+  return VX_OK;
+}
+
+int set_slot_fields(vx_handle* h, int slot, int mode, int token) {
+  SlotUpdate u{};
+  u.set_mode = 1; u.mode = mode; u.token = token;
+  return slot_update(h, slot, u);
+}
+
+int need_positions(vx_handle* h, int slot, int n) {
+  if (h->pos_host[slot] + n > h->cfg.max_seq_len)
+    return h->fail(VX_E_RANGE, "position %d + %d exceeds maxSeqLen %d", h->pos_host[slot], n, h->cfg.max_seq_len);
+  return VX_OK;
+}
+
+int finish(vx_handle* h) {
+  CK(cudaStreamSynchronize(h->stream));
+  return check_device_error(h);
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+extern "C" {
+
+void vx_default_config(vx_config* c) {
+  memset(c, 0, sizeof(*c));
+  c->dim = 3072; c->n_layers = 26; c->head_dim = 128; c->hidden_dim = 9216; c->n_heads = 32; c->n_kv_heads = 8;
+  c->vocab_size = 131072; c->rope_theta = 1.0e6f; c->norm_eps = 1e-5f;
+  c->fm_n_layers = 3; c->fm_nfe = 8; c->fm_cfg_alpha = 1.2f; c->fm_n_acoustic = 36; c->fm_semantic_vocab = 8320;
+  c->acoustic_levels = 21; c->audio_vocab = 9088;
+  c->max_seq_len = 4096; c->max_slots = 1; c->max_frames = 2048; c->max_voice_rows = 256;
+  c->enable_fm = 1; c->device = 0; c->tp_size = 1; c->tp_rank = 0;
+}
+
+const char* vx_last_error(const vx_handle* h) { return h ? h->err.c_str() : "null handle"; }
+
+int64_t vx_launch_count(const vx_handle* h) { return h ? h->launches : 0; }
+
+static void add_tensor(vx_handle* h, const std::string& name, __half* dst, long long ld, long long rows, long long cols,
+                       long long full_rows, long long full_cols, long long row0, long long col0, bool norm) {
+  h->tensors[name] = TensorSlot{dst, ld, rows, cols, full_rows, full_cols, row0, col0, norm};
+}
+
+int vx_create(const vx_config* cfg, vx_handle** out) {
+  if (!cfg || !out) return VX_E_INVALID;
+  *out = nullptr;
+  vx_handle* h = new vx_handle();
+  h->cfg = *cfg;
+  const vx_config& c = h->cfg;
+  auto bad = [&](const char* m) { h->err = m; return VX_E_INVALID; };
+  int rc = VX_OK;
+  if (c.dim != 3072 || c.head_dim != 128 || c.hidden_dim != 9216 || c.n_heads != 32 || c.n_kv_heads != 8)
+    rc = bad("this build is specialised for the Ministral-3B shape (dim 3072, 32/8 heads of 128, FFN 9216)");
+  else if (c.n_layers < 1 || c.max_seq_len < 1 || c.max_slots < 1 || c.max_frames < 1 || c.max_voice_rows < 0)
+    rc = bad("bad sizes");
+  else if (!(c.tp_size == 1 || c.tp_size == 2 || c.tp_size == 4 || c.tp_size == 8) || c.tp_rank < 0 ||
+           c.tp_rank >= c.tp_size)
+    rc = bad("tp_size must be 1, 2, 4 or 8 with 0 <= tp_rank < tp_size");
+  else if (c.fm_nfe < 2 || c.fm_n_acoustic != 36 || c.fm_semantic_vocab < 8194 || c.audio_vocab < 9022)
+    rc = bad("bad acoustic-transformer config");
+  if (rc) { *out = h; return rc; }
+
+  if (const char* e = getenv("VX_NO_PDL")) h->use_pdl = !(e[0] == '1');
+  h->dev = c.device;
+  if (cudaSetDevice(h->dev) != cudaSuccess) { *out = h; return h->fail(VX_E_CUDA, "cudaSetDevice(%d) failed", h->dev); }
+  cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->dev);
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, h->dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, h->dev);
+  if (major != 10) { *out = h; return h->fail(VX_E_CUDA, "needs an sm_100 (B200) GPU, found sm_%d%d", major, minor); }
+  if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    *out = h; return h->fail(VX_E_CUDA, "stream create failed");
+  }
+  h->stream = h->own_stream;
+
+  h->tp = c.tp_size; h->rank = c.tp_rank;
+  h->D = c.dim; h->L = c.n_layers; h->HD = c.head_dim; h->F = c.hidden_dim;
+  h->NH = c.n_heads / h->tp; h->NKV = c.n_kv_heads / h->tp;
+  h->QD = h->NH * h->HD; h->KVD = h->NKV * h->HD; h->QKVD = h->QD + 2 * h->KVD; h->Fl = h->F / h->tp;
+  h->V = c.vocab_size; h->AV = c.audio_vocab; h->SEMV = c.fm_semantic_vocab; h->FL = c.enable_fm ? c.fm_n_layers : 0;
+  h->B = c.max_slots;
+  const long long D = h->D;
+
+  // ---------------------------------------------------------- weight arena
+  const size_t layer_elems = (size_t)h->QKVD * D + D * (size_t)h->QD + 2 * (size_t)h->Fl * D + D * (size_t)h->Fl + 2 * D;
+  const size_t fm_layer_elems = (size_t)6144 * D + D * 4096 + 2 * (size_t)h->F * D + D * (size_t)h->F + 2 * D;
+  size_t elems = layer_elems * h->L + (size_t)h->V * D + (size_t)h->AV * D + D;
+  if (c.enable_fm)
+    elems += fm_layer_elems * h->FL + D * 36 + (size_t)(h->SEMV + D) * D + D * D + D + 36 * D;
+  h->arena_bytes = elems * 2 + 64 * 256 * (h->L + h->FL + 16);
+  if (cudaMalloc(&h->arena, h->arena_bytes) != cudaSuccess) {
+    *out = h; return h->fail(VX_E_NOMEM, "cannot allocate %.2f GB of weights", h->arena_bytes / 1e9);
+  }
+  uint8_t* cur = (uint8_t*)h->arena;
+  auto alloc_h = [&](size_t n) { return (__half*)carve(cur, n * 2); };
+  const long long Q = c.n_heads * (long long)c.head_dim, KV = c.n_kv_heads * (long long)c.head_dim, Fm = c.hidden_dim;
+  h->layers.resize(h->L);
+  for (int l = 0; l < h->L; ++l) {
+    LayerW& W = h->layers[l];
+    const std::string pre = "layers." + std::to_string(l) + ".";
+    W.wqkv = alloc_h((size_t)h->QKVD * D);
+    W.wo = alloc_h(D * (size_t)h->QD);
+    W.w13 = alloc_h(2 * (size_t)h->Fl * D);
+    W.w2 = alloc_h(D * (size_t)h->Fl);
+    W.attn_norm = alloc_h(D);
+    W.ffn_norm = alloc_h(D);
+    const long long r = h->rank;
+    add_tensor(h, pre + "attention.wq.weight", W.wqkv, D, h->QD, D, Q, D, r * h->QD, 0, false);
+    add_tensor(h, pre + "attention.wk.weight", W.wqkv + (size_t)h->QD * D, D, h->KVD, D, KV, D, r * h->KVD, 0, false);
+    add_tensor(h, pre + "attention.wv.weight", W.wqkv + (size_t)(h->QD + h->KVD) * D, D, h->KVD, D, KV, D,
+               r * h->KVD, 0, false);
+    add_tensor(h, pre + "attention.wo.weight", W.wo, h->QD, D, h->QD, D, Q, 0, r * h->QD, false);
+    add_tensor(h, pre + "feed_forward.w1.weight", W.w13, D, h->Fl, D, Fm, D, r * h->Fl, 0, false);
+    add_tensor(h, pre + "feed_forward.w3.weight", W.w13 + (size_t)h->Fl * D, D, h->Fl, D, Fm, D, r * h->Fl, 0, false);
+    add_tensor(h, pre + "feed_forward.w2.weight", W.w2, h->Fl, D, h->Fl, D, Fm, 0, r * h->Fl, false);
+    add_tensor(h, pre + "attention_norm.weight", W.attn_norm, D, 1, D, 1, D, 0, 0, true);
+    add_tensor(h, pre + "ffn_norm.weight", W.ffn_norm, D, 1, D, 1, D, 0, 0, true);
+  }
+  h->tok_emb = alloc_h((size_t)h->V * D);
+  h->audio_emb = alloc_h((size_t)h->AV * D);
+  h->final_norm = alloc_h(D);
+  add_tensor(h, "mm_audio_embeddings.tok_embeddings.weight", h->tok_emb, D, h->V, D, h->V, D, 0, 0, false);
+  add_tensor(h, "mm_audio_embeddings.audio_codebook_embeddings.embeddings.weight", h->audio_emb, D, h->AV, D, h->AV, D,
+             0, 0, false);
+  add_tensor(h, "norm.weight", h->final_norm, D, 1, D, 1, D, 0, 0, true);
+  if (c.enable_fm) {
+    const std::string p = "acoustic_transformer.";
+    h->fm_layers.resize(h->FL);
+    for (int l = 0; l < h->FL; ++l) {
+      LayerW& W = h->fm_layers[l];
+      const std::string pre = p + "layers." + std::to_string(l) + ".";
+      W.wqkv = alloc_h((size_t)6144 * D);
+      W.wo = alloc_h(D * 4096);
+      W.w13 = alloc_h(2 * (size_t)Fm * D);
+      W.w2 = alloc_h(D * (size_t)Fm);
+      W.attn_norm = alloc_h(D);
+      W.ffn_norm = alloc_h(D);
+      add_tensor(h, pre + "attention.wq.weight", W.wqkv, D, Q, D, Q, D, 0, 0, false);
+      add_tensor(h, pre + "attention.wk.weight", W.wqkv + (size_t)Q * D, D, KV, D, KV, D, 0, 0, false);
+      add_tensor(h, pre + "attention.wv.weight", W.wqkv + (size_t)(Q + KV) * D, D, KV, D, KV, D, 0, 0, false);
+      add_tensor(h, pre + "attention.wo.weight", W.wo, Q, D, Q, D, Q, 0, 0, false);
+      add_tensor(h, pre + "feed_forward.w1.weight", W.w13, D, Fm, D, Fm, D, 0, 0, false);
+      add_tensor(h, pre + "feed_forward.w3.weight", W.w13 + (size_t)Fm * D, D, Fm, D, Fm, D, 0, 0, false);
+      add_tensor(h, pre + "feed_forward.w2.weight", W.w2, Fm, D, Fm, D, Fm, 0, 0, false);
+      add_tensor(h, pre + "attention_norm.weight", W.attn_norm, D, 1, D, 1, D, 0, 0, true);
+      add_tensor(h, pre + "ffn_norm.weight", W.ffn_norm, D, 1, D, 1, D, 0, 0, true);
+    }
+    h->fm_in = alloc_h(D * 36);
+    h->fm_head = alloc_h((size_t)(h->SEMV + D) * D);
+    h->fm_time = alloc_h(D * D);
+    h->fm_norm = alloc_h(D);
+    h->fm_ac = alloc_h(36 * D);
+    add_tensor(h, p + "input_projection.weight", h->fm_in, 36, D, 36, D, 36, 0, 0, false);
+    add_tensor(h, p + "semantic_codebook_output.weight", h->fm_head, D, h->SEMV, D, h->SEMV, D, 0, 0, false);
+    add_tensor(h, p + "llm_projection.weight", h->fm_head + (size_t)h->SEMV * D, D, D, D, D, D, 0, 0, false);
+    add_tensor(h, p + "time_projection.weight", h->fm_time, D, D, D, D, D, 0, 0, false);
+    add_tensor(h, p + "norm.weight", h->fm_norm, D, 1, D, 1, D, 0, 0, true);
+    add_tensor(h, p + "acoustic_codebook_output.weight", h->fm_ac, D, 36, D, 36, D, 0, 0, false);
+  }
+
+  // ---------------------------------------------------------- KV cache + activations
+  h->max_pages = (c.max_seq_len + kPage - 1) / kPage;
+  const long long total_pages = (long long)h->B * h->max_pages;
+  h->kv_rows = total_pages * h->L * 2 * h->NKV * kPage;
+  h->n_splits = std::max(1, std::min(h->max_pages, (2 * h->num_sms + h->NKV - 1) / h->NKV));
+  size_t act = 0;
+  auto f32n = [&](size_t n) { act += ((n * 4 + 255) & ~size_t(255)); };
+  f32n(64);  // rope
+  f32n((size_t)h->B * D * 3 + (size_t)h->B * h->QD * 2 + (size_t)h->B * h->Fl);
+  f32n((size_t)h->B * h->NKV * h->n_splits * attn::kGqa * attn::kPartStride);
+  f32n((size_t)h->B * h->NKV);
+  f32n((size_t)h->B * c.max_seq_len);
+  f32n((size_t)h->B * c.max_voice_rows * D);
+  f32n((size_t)h->B * c.max_frames * 37);
+  f32n((size_t)h->B * c.max_frames * D);
+  f32n((size_t)h->V + 16);
+  f32n((size_t)(4 * h->L + 3) * D);
+  f32n((size_t)h->B * D);  // checkpoint normed
+  if (c.enable_fm) {
+    f32n((size_t)h->B * (h->SEMV + D));
+    f32n((size_t)h->B * 6 * D);
+    f32n((size_t)h->B * 6 * 6144);
+    f32n((size_t)h->B * 6 * 4096);
+    f32n((size_t)h->B * 6 * Fm);
+    f32n((size_t)h->B * (72 + 36 * 3));
+    f32n((size_t)8 * D + D);
+  }
+  act += 2 * ((sizeof(SlotState) * h->B + 255) & ~size_t(255));
+  act += ((size_t)h->B * h->max_pages * 4 + 255) & ~size_t(255);
+  void* abuf = nullptr;
+  if (cudaMalloc(&abuf, act + 4096) != cudaSuccess ||
+      cudaMalloc((void**)&h->kv_pool, (size_t)h->kv_rows * 256) != cudaSuccess) {
+    *out = h; return h->fail(VX_E_NOMEM, "cannot allocate KV cache (%.2f GB) / work buffers", h->kv_rows * 256 / 1e9);
+  }
+  cudaMemset(abuf, 0, act + 4096);
+  cudaMemset(h->kv_pool, 0, (size_t)h->kv_rows * 256);   // masked positions must hold finite values
+  uint8_t* ac = (uint8_t*)abuf;
+  auto fa = [&](size_t n) { return (float*)carve(ac, n * 4); };
+  h->rope_freq = fa(64);
+  h->h = fa((size_t)h->B * D); h->normed = fa((size_t)h->B * D); h->rows_in = fa((size_t)h->B * D);
+  h->q = fa((size_t)h->B * h->QD); h->att = fa((size_t)h->B * h->QD); h->g = fa((size_t)h->B * h->Fl);
+  h->attn_part = fa((size_t)h->B * h->NKV * h->n_splits * attn::kGqa * attn::kPartStride);
+  h->attn_tickets = (int*)fa((size_t)h->B * h->NKV);
+  h->prompt = (int32_t*)fa((size_t)h->B * c.max_seq_len);
+  h->voice = fa((size_t)h->B * c.max_voice_rows * D);
+  h->code_ring = (uint32_t*)fa((size_t)h->B * c.max_frames * 37);
+  h->normed_ring = fa((size_t)h->B * c.max_frames * D);
+  h->logits = fa((size_t)h->V + 16);
+  h->argmax_dev = (int32_t*)(h->logits + h->V);
+  h->dbg = fa((size_t)(4 * h->L + 3) * D);
+  h->ck_normed = fa((size_t)h->B * D);
+  if (c.enable_fm) {
+    h->fm_head_out = fa((size_t)h->B * (h->SEMV + D));
+    h->fm_seq = fa((size_t)h->B * 6 * D);
+    h->fm_qkv = fa((size_t)h->B * 6 * 6144);
+    h->fm_att = fa((size_t)h->B * 6 * 4096);
+    h->fm_g = fa((size_t)h->B * 6 * Fm);
+    float* small = fa((size_t)h->B * (72 + 36 * 3));
+    h->fm_vel = small; h->fm_x = small + (size_t)h->B * 72; h->fm_noise = h->fm_x + (size_t)h->B * 36;
+    h->fm_xfinal = h->fm_noise + (size_t)h->B * 36;
+    h->tp_table = fa((size_t)8 * D + D);
+    h->te_tmp = h->tp_table + (size_t)8 * D;
+  }
+  h->slots = (SlotState*)carve(ac, sizeof(SlotState) * h->B);
+  h->ck_slots = (SlotState*)carve(ac, sizeof(SlotState) * h->B);
+  h->page_table = (int32_t*)carve(ac, (size_t)h->B * h->max_pages * 4);
+
+  // rope frequencies 1/theta^(2i/head_dim), formed in double and rounded once
+  std::vector<float> freq(64, 0.f);
+  for (int i = 0; i < h->HD / 2; ++i) freq[i] = (float)(1.0 / pow((double)c.rope_theta, (double)(2 * i) / h->HD));
+  std::vector<int32_t> ptab((size_t)h->B * h->max_pages);
+  for (size_t i = 0; i < ptab.size(); ++i) ptab[i] = (int32_t)i;   // slot s owns pages [s*max_pages, (s+1)*max_pages)
+  std::vector<SlotState> st(h->B);
+  memset(st.data(), 0, sizeof(SlotState) * h->B);
+  for (int s = 0; s < h->B; ++s) {
+    st[s].max_frames = c.max_frames;
+    st[s].codes_key = vx_stream_key(VX_SEED_CODES, s);
+    st[s].noise_key = vx_stream_key(VX_SEED_FM_NOISE, s);
+  }
+  if (cudaMemcpy(h->rope_freq, freq.data(), 64 * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(h->page_table, ptab.data(), ptab.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(h->slots, st.data(), sizeof(SlotState) * h->B, cudaMemcpyHostToDevice) != cudaSuccess) {
+    *out = h; return h->fail(VX_E_CUDA, "init copies failed");
+  }
+  h->pinned_bytes = std::max<size_t>((size_t)(4 * h->L + 3) * D * 4, (size_t)(h->SEMV + 64) * 4) + (size_t)c.max_frames * 37 * 4 +
+                    (size_t)c.max_seq_len * 4 + 65536;
+  if (cudaMallocHost(&h->pinned, h->pinned_bytes) != cudaSuccess) { *out = h; return h->fail(VX_E_NOMEM, "pinned"); }
+  h->pos_host.assign(h->B, 0); h->frame_host.assign(h->B, 0); h->prompt_len_host.assign(h->B, 0);
+  h->ck_pos_host.assign(h->B, 0);
+  h->ck_frame_host.assign(h->B, 0);
+  h->g_step.resize(h->B); h->g_fm.resize(h->B); h->g_frame_fm.resize(h->B); h->g_frame_bb.resize(h->B);
+  if ((rc = make_kv_map(h))) { *out = h; return rc; }
+  if ((rc = prime_kernel_attrs(h))) { *out = h; return rc; }
+  *out = h;
+  return VX_OK;
+}
+
+void vx_destroy(vx_handle* h) {
+  if (!h) return;
+  cudaSetDevice(h->dev);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  for (auto* tab : {&h->g_step, &h->g_fm, &h->g_frame_fm, &h->g_frame_bb})
+    for (auto& g : *tab)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+  if (h->comm && g_nccl.commDestroy) g_nccl.commDestroy(h->comm);
+  if (h->arena) cudaFree(h->arena);
+  if (h->kv_pool) cudaFree(h->kv_pool);
+  if (h->rope_freq) cudaFree(h->rope_freq);   // base of the activation block
+  if (h->pinned) cudaFreeHost(h->pinned);
+  if (h->own_stream) cudaStreamDestroy(h->own_stream);
+  delete h;
+}
+
+int vx_set_stream(vx_handle* h, void* stream) {
+  if (!h) return VX_E_INVALID;
+  h->stream = stream ? (cudaStream_t)stream : h->own_stream;
+  return VX_OK;
+}
+
+int vx_synchronize(vx_handle* h) {
+  if (!h) return VX_E_INVALID;
+  cudaSetDevice(h->dev);
+  return finish(h);
+}
+
+int vx_init_random_weights(vx_handle* h, uint64_t seed) {
+  if (!h || !h->arena) return VX_E_STATE;
+  CK(cudaSetDevice(h->dev));
+  for (auto& kv : h->tensors) {
+    const TensorSlot& t = kv.second;
+    if (t.is_norm) {
+      k_fill_f16<<<4, 256, 0, h->stream>>>(t.dst, t.cols, 1.0f);
+      CK(cudaGetLastError());
+      continue;
+    }
+    const uint64_t key = vx_stream_key(seed, vx_fnv1a(kv.first.c_str()));
+    if (t.cols == t.full_cols && t.ld == t.cols) {
+      // the block spans whole rows: element i is element row0*C + i of the full tensor
+      k_init_normal_f16_off<<<2048, 256, 0, h->stream>>>(t.dst, t.rows * t.cols, t.row0 * t.full_cols, key,
+                                                         VX_WEIGHT_SIGMA);
+      CK(cudaGetLastError());
+    } else {
+      for (long long r = 0; r < t.rows; ++r) {
+        k_init_normal_f16_off<<<(int)std::min(1024LL, t.cols / 256 + 1), 256, 0, h->stream>>>(
+            t.dst + r * t.ld, t.cols, (t.row0 + r) * t.full_cols + t.col0, key, VX_WEIGHT_SIGMA);
+        CK(cudaGetLastError());
+      }
+    }
+  }
+  CK(cudaStreamSynchronize(h->stream));
+  h->weights_ready = true;
+  if (h->cfg.enable_fm) return build_tp_table(h);
+  return VX_OK;
+}
+
+size_t vx_tensor_numel(const vx_handle* h, const char* name) {
+  if (!h || !name) return 0;
+  auto it = h->tensors.find(name);
+  if (it == h->tensors.end()) return 0;
+  return (size_t)(it->second.full_rows * it->second.full_cols);
+}
+
+int vx_load_tensor(vx_handle* h, const char* name, const uint16_t* f16, size_t n) {
+  if (!h || !name || !f16) return VX_E_INVALID;
+  auto it = h->tensors.find(name);
+  if (it == h->tensors.end()) return h->fail(VX_E_INVALID, "Missing weight: %s", name);
+  const TensorSlot& t = it->second;
+  if ((long long)n != t.full_rows * t.full_cols)
+    return h->fail(VX_E_INVALID, "%s: expected %lld elements, got %zu", name, t.full_rows * t.full_cols, n);
+  CK(cudaSetDevice(h->dev));
+  const uint16_t* src = f16 + t.row0 * t.full_cols + t.col0;
+  CK(cudaMemcpy2D(t.dst, t.ld * 2, src, t.full_cols * 2, t.cols * 2, t.rows, cudaMemcpyHostToDevice));
+  return VX_OK;
+}
+
+int vx_read_tensor(vx_handle* h, const char* name, uint16_t* out, size_t n) {
+  if (!h || !name || !out) return VX_E_INVALID;
+  auto it = h->tensors.find(name);
+  if (it == h->tensors.end()) return h->fail(VX_E_INVALID, "Missing weight: %s", name);
+  const TensorSlot& t = it->second;
+  if (t.rows != t.full_rows || t.cols != t.full_cols) return h->fail(VX_E_STATE, "tensor is sharded");
+  if ((long long)n != t.rows * t.cols) return h->fail(VX_E_INVALID, "size mismatch");
+  CK(cudaSetDevice(h->dev));
+  CK(cudaMemcpy2D(out, t.cols * 2, t.dst, t.ld * 2, t.cols * 2, t.rows, cudaMemcpyDeviceToHost));
+  return VX_OK;
+}
+
+int vx_mark_weights_loaded(vx_handle* h) {
+  if (!h) return VX_E_INVALID;
+  h->weights_ready = true;
+  if (h->cfg.enable_fm) return build_tp_table(h);
+  return VX_OK;
+}
+
+int vx_reset(vx_handle* h, int32_t slot) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->dev));
+  SlotUpdate u{};
+  u.set_counters = 1;   // pos = frame = 0
+  if ((rc = slot_update(h, slot, u))) return rc;
+  h->pos_host[slot] = 0;
+  h->frame_host[slot] = 0;
+  return finish(h);
+}
+
+int vx_get_position(vx_handle* h, int32_t slot, int32_t* pos) {
+  if (!h || !pos) return VX_E_INVALID;
+  if (slot < 0 || slot >= h->B) return h->fail(VX_E_RANGE, "slot out of range");
+  *pos = h->pos_host[slot];
+  return VX_OK;
+}
+
+int vx_set_streams(vx_handle* h, int32_t slot, uint64_t noise_seed, uint64_t codes_seed, int32_t utt) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->dev));
+  SlotUpdate u{};
+  u.set_keys = 1;
+  u.noise_key = vx_stream_key(noise_seed, (uint64_t)utt);
+  u.codes_key = vx_stream_key(codes_seed, (uint64_t)utt);
+  u.set_noise_mode = 1;
+  u.noise_mode = 0;
+  if ((rc = slot_update(h, slot, u))) return rc;
+  return finish(h);
+}
+
+int vx_prefill(vx_handle* h, int32_t slot, const int32_t* tokens, int32_t n, int32_t audio_start, int32_t audio_count,
+               const float* voice) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (!tokens || n < 0) return h->fail(VX_E_INVALID, "tokens");
+  if (audio_count < 0 || (audio_count > 0 && (!voice || audio_start < 0 || audio_start + audio_count > n)))
+    return h->fail(VX_E_INVALID, "voice span [%d, %d) does not fit the prompt", audio_start, audio_start + audio_count);
+  if (voice && audio_count > h->cfg.max_voice_rows)
+    return h->fail(VX_E_RANGE, "%d voice rows exceed max_voice_rows %d", audio_count, h->cfg.max_voice_rows);
+  if ((rc = need_positions(h, slot, n))) return rc;
+  CK(cudaSetDevice(h->dev));
+  const int p0 = h->pos_host[slot];
+  std::vector<int32_t> pt(n);
+  for (int i = 0; i < n; ++i) {
+    const bool is_voice = voice && i >= audio_start && i < audio_start + audio_count;
+    if (!is_voice && (tokens[i] < 0 || tokens[i] >= h->V)) return h->fail(VX_E_RANGE, "token %d out of range", tokens[i]);
+    pt[i] = is_voice ? -(i - audio_start) - 1 : tokens[i];
+  }
+  if (n == 0) return VX_OK;
+  // pageable sources: cudaMemcpyAsync stages them before returning, ordered in the stream
+  CK(cudaMemcpyAsync(h->prompt + (size_t)slot * h->cfg.max_seq_len + p0, pt.data(), (size_t)n * 4,
+                     cudaMemcpyHostToDevice, h->stream));
+  if (voice && audio_count)
+    CK(cudaMemcpyAsync(h->voice + (size_t)slot * h->cfg.max_voice_rows * h->D, voice, (size_t)audio_count * h->D * 4,
+                       cudaMemcpyHostToDevice, h->stream));
+  SlotUpdate u{};
+  u.set_mode = 1; u.mode = kEmbPrompt; u.token = 0;
+  u.set_prompt_len = 1; u.prompt_len = p0 + n;
+  if ((rc = slot_update(h, slot, u))) return rc;
+  for (int i = 0; i < n; ++i)
+    if ((rc = run_prog(h, kProgStep, slot))) return rc;
+  h->pos_host[slot] += n;
+  return finish(h);
+}
+
+static int step_common(vx_handle* h, int slot, float* normed_out, int32_t* argmax_out) {
+  int rc;
+  if ((rc = run_prog(h, kProgStep, slot))) return rc;
+  h->pos_host[slot] += 1;
+  if (argmax_out) {
+    gemv::Params p{};
+    p.W = h->tok_emb; p.ldw = h->D; p.rows = h->V; p.col0 = 0; p.kc = h->D;
+    p.x = h->normed + (size_t)slot * h->D; p.ldx = h->D; p.y = h->logits; p.ldy = 0;
+    if ((rc = run_gemv<1, 6, 3, gemv::kStore, false>(h, p))) return rc;
+    CK(launch(h, k_argmax, dim3(1), dim3(1024), 0, (const float*)h->logits, h->V, h->argmax_dev));
+    CK(cudaMemcpyAsync(h->pinned, h->argmax_dev, 4, cudaMemcpyDeviceToHost, h->stream));
+  }
+  if (normed_out)
+    CK(cudaMemcpyAsync(h->pinned + 64, h->normed + (size_t)slot * h->D, (size_t)h->D * 4, cudaMemcpyDeviceToHost,
+                       h->stream));
+  if ((rc = finish(h))) return rc;
+  if (argmax_out) memcpy(argmax_out, h->pinned, 4);
+  if (normed_out) memcpy(normed_out, h->pinned + 64, (size_t)h->D * 4);
+  return VX_OK;
+}
+
+int vx_backbone_step(vx_handle* h, int32_t slot, int32_t token, int32_t use_audio, const float* embed,
+                     float* normed_out, int32_t* argmax_out) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if ((rc = need_positions(h, slot, 1))) return rc;
+  if (!embed && (token < 0 || token >= (use_audio ? h->AV : h->V)))
+    return h->fail(VX_E_RANGE, "token %d out of range", token);
+  CK(cudaSetDevice(h->dev));
+  if (embed) {
+    CK(cudaMemcpyAsync(h->rows_in + (size_t)slot * h->D, embed, (size_t)h->D * 4, cudaMemcpyHostToDevice, h->stream));
+    if ((rc = set_slot_fields(h, slot, kEmbRow, 0))) return rc;
+  } else if ((rc = set_slot_fields(h, slot, use_audio ? kEmbAudioToken : kEmbToken, token))) {
+    return rc;
+  }
+  return step_common(h, slot, normed_out, argmax_out);
+}
+
+int vx_backbone_step_codes(vx_handle* h, int32_t slot, uint32_t sem, const uint32_t* ac, float* normed_out) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (!ac) return h->fail(VX_E_INVALID, "acoustic codes");
+  if ((rc = need_positions(h, slot, 1))) return rc;
+  if ((int)sem >= h->AV) return h->fail(VX_E_RANGE, "semantic code %u out of range", sem);
+  for (int k = 0; k < 36; ++k)
+    if (8194 + 23 * k + (int)ac[k] >= h->AV) return h->fail(VX_E_RANGE, "acoustic code %u out of range", ac[k]);
+  CK(cudaSetDevice(h->dev));
+  SlotUpdate u{};
+  u.set_codes = 1;
+  u.codes[0] = sem;
+  memcpy(u.codes + 1, ac, 36 * 4);
+  u.set_mode = 1; u.mode = kEmbCodes; u.token = 0;
+  if ((rc = slot_update(h, slot, u))) return rc;
+  return step_common(h, slot, normed_out, nullptr);
+}
+
+int vx_fm_step(vx_handle* h, int32_t slot, const float* noise, float* sem_logits, uint32_t* sem_code,
+               uint32_t* ac_codes, float* x_final) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (!h->cfg.enable_fm) return h->fail(VX_E_STATE, "engine created without the acoustic transformer");
+  CK(cudaSetDevice(h->dev));
+  {
+    SlotUpdate u{};
+    u.set_noise_mode = 1;
+    u.noise_mode = noise ? 1 : 0;
+    if ((rc = slot_update(h, slot, u))) return rc;
+  }
+  if (noise)
+    CK(cudaMemcpyAsync(h->fm_noise + (size_t)slot * 36, noise, 36 * 4, cudaMemcpyHostToDevice, h->stream));
+  if ((rc = run_prog(h, kProgFm, slot))) return rc;
+  // frame counter advanced by the FM tail: the codes of this call are in ring row frame_host
+  const int fr = h->frame_host[slot];
+  uint8_t* pb = h->pinned + 1024;
+  const size_t nl = (size_t)h->SEMV * 4;
+  CK(cudaMemcpyAsync(pb, h->fm_head_out + (size_t)slot * (h->SEMV + h->D), nl, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaMemcpyAsync(pb + nl, reinterpret_cast<uint8_t*>(&h->slots[slot]) + offsetof(SlotState, codes), 37 * 4,
+                     cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaMemcpyAsync(pb + nl + 256, h->fm_xfinal + (size_t)slot * 36, 36 * 4, cudaMemcpyDeviceToHost, h->stream));
+  if ((rc = finish(h))) return rc;
+  h->frame_host[slot] = fr + 1;
+  if (noise) {  // back to the seeded stream for device-resident decode
+    SlotUpdate u{};
+    u.set_noise_mode = 1;
+    u.noise_mode = 0;
+    if ((rc = slot_update(h, slot, u))) return rc;
+  }
+  const uint32_t* codes = reinterpret_cast<const uint32_t*>(pb + nl);
+  if (sem_logits) memcpy(sem_logits, pb, nl);
+  if (sem_code) *sem_code = codes[0];
+  if (ac_codes) memcpy(ac_codes, codes + 1, 36 * 4);
+  if (x_final) memcpy(x_final, pb + nl + 256, 36 * 4);
+  return VX_OK;
+}
+
+int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (!out) return h->fail(VX_E_INVALID, "out");
+  if (token < 0 || token >= h->V) return h->fail(VX_E_RANGE, "token out of range");
+  if ((rc = need_positions(h, slot, 1))) return rc;
+  CK(cudaSetDevice(h->dev));
+  if ((rc = set_slot_fields(h, slot, kEmbToken, token))) return rc;
+  DebugSink sink{h->dbg};
+  if ((rc = enqueue_backbone(h, slot, false, false, &sink))) return rc;
+  h->pos_host[slot] += 1;
+  const size_t n = (size_t)(4 * h->L + 3) * h->D;
+  CK(cudaMemcpyAsync(out, h->dbg, n * 4, cudaMemcpyDeviceToHost, h->stream));
+  return finish(h);
+}
+
+int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (n_frames < 0) return h->fail(VX_E_INVALID, "n_frames");
+  if (with_fm && !h->cfg.enable_fm) return h->fail(VX_E_STATE, "engine created without the acoustic transformer");
+  int f0 = h->frame_host[slot];
+  if (f0 + n_frames > h->cfg.max_frames)
+    return h->fail(VX_E_RANGE, "frames %d + %d exceed the code ring (%d)", f0, n_frames, h->cfg.max_frames);
+  // backbone steps this call will run
+  const int steps = with_fm ? (f0 == 0 ? std::max(0, n_frames - 1) : n_frames) : n_frames;
+  if ((rc = need_positions(h, slot, steps))) return rc;
+  CK(cudaSetDevice(h->dev));
+  for (int i = 0; i < n_frames; ++i) {
+    const int f = f0 + i;
+    if (with_fm) {
+      if (f == 0) {
+        if ((rc = run_prog(h, kProgFm, slot))) return rc;
+      } else {
+        if (i == 0 || f0 + i == 1) {
+          if ((rc = set_slot_fields(h, slot, kEmbCodes, 0))) return rc;
+        }
+        if ((rc = run_prog(h, kProgFrameFm, slot))) return rc;
+        h->pos_host[slot] += 1;
+      }
+    } else {
+      if (f == 0) {
+        if ((rc = set_slot_fields(h, slot, kEmbToken, kAudioKick))) return rc;
+      } else if (i == 0 || f == 1) {
+        if ((rc = set_slot_fields(h, slot, kEmbSynthCodes, 0))) return rc;
+      }
+      if ((rc = run_prog(h, kProgFrameBb, slot))) return rc;
+      h->pos_host[slot] += 1;
+    }
+  }
+  h->frame_host[slot] = f0 + n_frames;
+  return VX_OK;
+}
+
+int vx_read_codes(vx_handle* h, int32_t slot, int32_t frame0, int32_t n, uint32_t* out) {
+  if (!h || !out) return VX_E_INVALID;
+  if (slot < 0 || slot >= h->B || frame0 < 0 || n < 0 || frame0 + n > h->cfg.max_frames)
+    return h->fail(VX_E_RANGE, "frame range");
+  CK(cudaSetDevice(h->dev));
+  CK(cudaMemcpyAsync(out, h->code_ring + ((size_t)slot * h->cfg.max_frames + frame0) * 37, (size_t)n * 37 * 4,
+                     cudaMemcpyDeviceToHost, h->stream));
+  return finish(h);
+}
+
+int vx_read_normed(vx_handle* h, int32_t slot, int32_t frame0, int32_t n, float* out) {
+  if (!h || !out) return VX_E_INVALID;
+  if (slot < 0 || slot >= h->B || frame0 < 0 || n < 0 || frame0 + n > h->cfg.max_frames)
+    return h->fail(VX_E_RANGE, "frame range");
+  CK(cudaSetDevice(h->dev));
+  CK(cudaMemcpyAsync(out, h->normed_ring + ((size_t)slot * h->cfg.max_frames + frame0) * h->D, (size_t)n * h->D * 4,
+                     cudaMemcpyDeviceToHost, h->stream));
+  return finish(h);
+}
+
+int vx_checkpoint(vx_handle* h, int32_t slot) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->dev));
+  CK(cudaMemcpyAsync(&h->ck_slots[slot], &h->slots[slot], sizeof(SlotState), cudaMemcpyDeviceToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->ck_normed + (size_t)slot * h->D, h->normed + (size_t)slot * h->D, (size_t)h->D * 4,
+                     cudaMemcpyDeviceToDevice, h->stream));
+  h->ck_pos_host[slot] = h->pos_host[slot];
+  h->ck_frame_host[slot] = h->frame_host[slot];
+  return finish(h);
+}
+
+int vx_rewind(vx_handle* h, int32_t slot) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  CK(cudaSetDevice(h->dev));
+  CK(cudaMemcpyAsync(&h->slots[slot], &h->ck_slots[slot], sizeof(SlotState), cudaMemcpyDeviceToDevice, h->stream));
+  CK(cudaMemcpyAsync(h->normed + (size_t)slot * h->D, h->ck_normed + (size_t)slot * h->D, (size_t)h->D * 4,
+                     cudaMemcpyDeviceToDevice, h->stream));
+  h->pos_host[slot] = h->ck_pos_host[slot];
+  h->frame_host[slot] = h->ck_frame_host[slot];
+  return VX_OK;
+}
+
+int vx_nccl_unique_id(const char* lib, uint8_t out[128]) {
+  std::string err;
+  if (!out || !g_nccl.load(lib, err)) return VX_E_NCCL;
+  ncclUniqueId id;
+  if (g_nccl.getUniqueId(&id) != ncclSuccess) return VX_E_NCCL;
+  memcpy(out, id.internal, 128);
+  return VX_OK;
+}
+
+int vx_tp_init(vx_handle* h, const char* lib, const uint8_t id_bytes[128]) {
+  if (!h || !id_bytes) return VX_E_INVALID;
+  if (h->tp == 1) return VX_OK;
+  std::string err;
+  if (!g_nccl.load(lib, err)) return h->fail(VX_E_NCCL, "%s", err.c_str());
+  CK(cudaSetDevice(h->dev));
+  ncclUniqueId id;
+  memcpy(id.internal, id_bytes, 128);
+  ncclResult_t r = g_nccl.commInitRank(&h->comm, h->tp, id, h->rank);
+  if (r != ncclSuccess) return h->fail(VX_E_NCCL, "ncclCommInitRank: %s", g_nccl.getErrorString(r));
+  return VX_OK;
+}
+
+}  // extern "C"
+
