@@ -169,6 +169,14 @@ int vx_synchronize(vx_handle* h);
  * the kernels they contain). */
 int64_t vx_launch_count(const vx_handle* h);
 
+/* Measurement: runs `reps` backbone steps of the slot kernel by kernel (no
+ * programmatic overlap) with a CUDA event pair around every launch.  out_ms[3] =
+ * average ms per step spent in {weight-streaming GEMVs, attention, other kernels};
+ * out_bytes[1] = algorithmic bytes the GEMVs move per step.  Advances the
+ * position by `reps` (use vx_checkpoint / vx_rewind around it).  No counterpart in
+ * the reference (its benchmark times whole submits, src/benchmark.ts:288-292). */
+int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, double* out_bytes);
+
 /* Tensor parallelism over NCCL (batch-1 latency, heads and FFN columns
  * sharded): the unique id comes from vx_nccl_unique_id on rank 0 and is shared by
  * the host (e.g. torch.distributed).  nccl_lib: path of libnccl.so.2 (NULL: the

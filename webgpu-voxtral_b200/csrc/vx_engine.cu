@@ -144,6 +144,13 @@ struct vx_handle {
   // TP
   ncclComm_t comm = nullptr;
 
+  // per-kernel profiling (vx_profile_step): category of the next launch, events, bytes
+  bool profiling = false;
+  int cur_cat = 2;
+  struct ProfEv { cudaEvent_t a, b; int cat; };
+  std::vector<ProfEv> prof;
+  double prof_bytes[3] = {0, 0, 0};
+
   int fail(int code, const char* fmt, ...) {
     char buf[512];
     va_list ap;
@@ -176,7 +183,16 @@ cudaError_t launch(vx_handle* h, void (*kern)(KArgs...), dim3 grid, dim3 block, 
   cfg.attrs = at;
   cfg.numAttrs = h->use_pdl ? 1 : 0;
   h->launches++;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (!h->profiling) return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  vx_handle::ProfEv ev{nullptr, nullptr, h->cur_cat};
+  cudaEventCreate(&ev.a);
+  cudaEventCreate(&ev.b);
+  cudaEventRecord(ev.a, h->stream);
+  cudaError_t r = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  cudaEventRecord(ev.b, h->stream);
+  h->prof.push_back(ev);
+  h->cur_cat = 2;
+  return r;
 }
 
 template <int M, int R, int CPL, int EPI, bool NORM>
@@ -215,6 +231,13 @@ int run_gemv(vx_handle* h, const gemv::Params& p) {
                    p.ldw, CPL, R);
   const int ntiles = (p.rows + ORT - 1) / ORT;
   const int grid = std::min(ntiles, h->num_sms);
+  if (h->profiling) {
+    // algorithmic bytes: the weight slice once, x once, y written (read too for residual adds)
+    const double w = (double)p.rows * p.kc * 2.0 * (EPI == gemv::kSwiglu ? 2.0 : 1.0);
+    const double xy = (double)M * p.kc * 4.0 + (double)M * p.rows * 4.0 * (EPI == gemv::kResid ? 2.0 : 1.0);
+    h->prof_bytes[0] += w + xy;
+    h->cur_cat = 0;
+  }
   CK(launch(h, kern, dim3(grid), dim3(gemv::kThreads), gemv::kSmemBytes, p));
   return VX_OK;
 }
@@ -312,6 +335,7 @@ int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const 
       ap.tickets = h->attn_tickets + (long long)slot * h->NKV;
       ap.kv = kg; ap.layer = l; ap.pos = &h->slots[0].pos; ap.pos_stride = kPosStride; ap.slot0 = slot;
       ap.n_splits = h->n_splits; ap.scale = 1.0f / sqrtf((float)h->HD);
+      h->cur_cat = 1;
       CK(launch(h, attn::k_attn_decode, dim3(h->NKV, h->n_splits, 1), dim3(attn::kThreads), attn::kSmemBytes,
                 h->kv_map, ap));
     }
@@ -1122,6 +1146,40 @@ int vx_rewind(vx_handle* h, int32_t slot) {
   h->pos_host[slot] = h->ck_pos_host[slot];
   h->frame_host[slot] = h->ck_frame_host[slot];
   return VX_OK;
+}
+
+int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, double* out_bytes) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (!out_ms || reps < 1) return h->fail(VX_E_INVALID, "profile args");
+  if ((rc = need_positions(h, slot, reps))) return rc;
+  CK(cudaSetDevice(h->dev));
+  const bool pdl = h->use_pdl;
+  h->use_pdl = false;            // events must bracket exactly one kernel
+  h->profiling = true;
+  h->prof.clear();
+  h->prof_bytes[0] = h->prof_bytes[1] = h->prof_bytes[2] = 0;
+  for (int i = 0; i < reps && rc == VX_OK; ++i) {
+    rc = set_slot_fields(h, slot, kEmbSynthCodes, 0);
+    if (!rc) rc = enqueue_backbone(h, slot, false, false, nullptr);
+    if (!rc) h->pos_host[slot] += 1;
+  }
+  h->profiling = false;
+  h->use_pdl = pdl;
+  cudaError_t se = cudaStreamSynchronize(h->stream);
+  float acc[3] = {0, 0, 0};
+  for (auto& ev : h->prof) {
+    float ms = 0.f;
+    if (se == cudaSuccess && cudaEventElapsedTime(&ms, ev.a, ev.b) == cudaSuccess) acc[ev.cat] += ms;
+    cudaEventDestroy(ev.a);
+    cudaEventDestroy(ev.b);
+  }
+  h->prof.clear();
+  if (rc) return rc;
+  if (se != cudaSuccess) return h->fail(VX_E_CUDA, "profile: %s", cudaGetErrorString(se));
+  for (int k = 0; k < 3; ++k) out_ms[k] = acc[k] / reps;
+  if (out_bytes) out_bytes[0] = h->prof_bytes[0] / reps;
+  return check_device_error(h);
 }
 
 int vx_nccl_unique_id(const char* lib, uint8_t out[128]) {

@@ -99,6 +99,8 @@ def load_library():
         "vx_set_stream": (ctypes.c_int, [H, ctypes.c_void_p]),
         "vx_synchronize": (ctypes.c_int, [H]),
         "vx_launch_count": (ctypes.c_int64, [H]),
+        "vx_profile_step": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p,
+                                           ctypes.POINTER(ctypes.c_double)]),
         "vx_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p, _u8p]),
         "vx_tp_init": (ctypes.c_int, [H, ctypes.c_char_p, _u8p]),
     }
@@ -254,6 +256,14 @@ class VoxtralEngine:
 
     def rewind(self, slot: int = 0):
         self._check(load_library().vx_rewind(self._h, slot))
+
+    def profile_step(self, reps: int = 4, slot: int = 0) -> dict:
+        """Per-category kernel time of one backbone step (CUDA events around each launch)."""
+        ms = np.zeros(3, np.float32)
+        by = ctypes.c_double()
+        self._check(load_library().vx_profile_step(self._h, slot, reps, _p(ms, _f32p), ctypes.byref(by)))
+        return {"gemv_ms": float(ms[0]), "attn_ms": float(ms[1]), "other_ms": float(ms[2]),
+                "gemv_bytes": float(by.value)}
 
     # ------------------------------------------------------------------ steps
     def prefill(self, tokens, audioTokenStart: int = 0, audioTokenCount: int = 0, voiceEmbeddings=None, slot: int = 0):
