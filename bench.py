@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--layers", type=int, default=26)
+    ap.add_argument("--text", type=int, default=N_TEXT, help="text ids in the prompt (C2: 512)")
+    ap.add_argument("--voice", type=int, default=N_VOICE, help="voice rows in the prompt (C2: 100)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -190,8 +192,8 @@ def run_b200(args):
     stream = torch.cuda.current_stream()
     eng.set_stream(stream.cuda_stream)
     utt = rank
-    toks, a0, na = synth.prompt(utt, N_TEXT, N_VOICE)
-    voice = synth.voice_rows(utt, N_VOICE)
+    toks, a0, na = synth.prompt(utt, args.text, args.voice)
+    voice = synth.voice_rows(utt, args.voice)
     eng.set_streams(3, 4, utt)
     eng.reset()
     eng.prefill(toks, a0, na, voice)
