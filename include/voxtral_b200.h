@@ -169,12 +169,13 @@ int vx_synchronize(vx_handle* h);
  * the kernels they contain). */
 int64_t vx_launch_count(const vx_handle* h);
 
-/* Measurement: runs `reps` backbone steps of the slot kernel by kernel (no
- * programmatic overlap) with a CUDA event pair around every launch.  out_ms[3] =
- * average ms per step spent in {weight-streaming GEMVs, attention, other kernels};
- * out_bytes[1] = algorithmic bytes the GEMVs move per step.  Advances the
- * position by `reps` (use vx_checkpoint / vx_rewind around it).  No counterpart in
- * the reference (its benchmark times whole submits, src/benchmark.ts:288-292). */
+/* Measurement: captures three variants of one backbone step of the slot as CUDA
+ * graphs — the full step, only its weight-streaming GEMVs, only its attention
+ * kernels — and times `reps` back-to-back launches of each with CUDA events on the
+ * handle's stream.  out_ms[3] = ms per step of {full, GEMV chain, attention chain};
+ * out_bytes[1] = algorithmic bytes the GEMVs of one step move.  The slot's state is
+ * restored afterwards.  No counterpart in the reference (its benchmark times whole
+ * submits with the CPU clock, src/benchmark.ts:288-292). */
 int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, double* out_bytes);
 
 /* Tensor parallelism over NCCL (batch-1 latency, heads and FFN columns

@@ -27,6 +27,7 @@ constexpr int kHd = 128;
 constexpr int kPage = 64;
 constexpr int kStageBytes = 4 * 8192;  // K box0, K box1, V box0, V box1 (64 rows x 64 cols f16 each)
 constexpr int kPartStride = 2 + kHd;   // (m, l, o[128]) per head
+constexpr int kMaxSplits = 64;         // splits per (row, kv head); the combine holds one weight per split
 constexpr size_t kSmemBytes = 2 * (size_t)kStageBytes + 1024 /*align slack*/ + 64;
 
 struct Params {
@@ -248,22 +249,42 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const __grid_constant_
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // ---- last split CTA: merge all splits of this (row, kv head) into attn_out
+  // ---- last split CTA: merge the splits that hold positions into attn_out.
+  // Warp h reduces head h's (max, sum) over the splits in parallel; then every
+  // thread sums its (head, dim) outputs with independent loads.
   const float* pb = p.part + ((long long)row * p.kv.n_kv + kvh) * p.n_splits * (kGqa * kPartStride);
+  const int n_used = min(p.n_splits, (npages + pps - 1) / pps);
+  __shared__ float s_w[kMaxSplits][kGqa];
+  {
+    const int h = warp;
+    float ms[2], ls[2];
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int sp = lane + 32 * j;
+      ms[j] = sp < n_used ? __ldcg(pb + sp * kGqa * kPartStride + h * kPartStride) : -INFINITY;
+      ls[j] = sp < n_used ? __ldcg(pb + sp * kGqa * kPartStride + h * kPartStride + 1) : 0.f;
+      M = fmaxf(M, ms[j]);
+    }
+    M = warp_max(M);
+    float f[2], L = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      f[j] = (ms[j] == -INFINITY) ? 0.f : expf(ms[j] - M);
+      L += ls[j] * f[j];
+    }
+    L = warp_sum(L);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (lane + 32 * j < n_used) s_w[lane + 32 * j][h] = f[j] / L;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < kGqa * kHd; idx += kThreads) {
     const int h = idx / kHd, d = idx % kHd;
-    float M = -INFINITY;
-    for (int sp = 0; sp < p.n_splits; ++sp) M = fmaxf(M, __ldcg(pb + sp * kGqa * kPartStride + h * kPartStride));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < p.n_splits; ++sp) {
-      const float* ps = pb + sp * kGqa * kPartStride + h * kPartStride;
-      const float ms = __ldcg(ps);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      L += __ldcg(ps + 1) * f;
-      O += __ldcg(ps + 2 + d) * f;
-    }
-    p.out[(long long)row * p.ldo + (long long)(kvh * kGqa + h) * kHd + d] = O / L;
+    float O = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < n_used; ++sp) O += __ldcg(pb + sp * kGqa * kPartStride + h * kPartStride + 2 + d) * s_w[sp][h];
+    p.out[(long long)row * p.ldo + (long long)(kvh * kGqa + h) * kHd + d] = O;
   }
   if (threadIdx.x == 0) p.tickets[row * p.kv.n_kv + kvh] = 0;
 }

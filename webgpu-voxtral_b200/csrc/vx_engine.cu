@@ -144,12 +144,10 @@ struct vx_handle {
   // TP
   ncclComm_t comm = nullptr;
 
-  // per-kernel profiling (vx_profile_step): category of the next launch, events, bytes
+  // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
+  int parts = 7;          // kPartMisc | kPartGemv | kPartAttn
   bool profiling = false;
-  int cur_cat = 2;
-  struct ProfEv { cudaEvent_t a, b; int cat; };
-  std::vector<ProfEv> prof;
-  double prof_bytes[3] = {0, 0, 0};
+  double prof_bytes = 0;
 
   int fail(int code, const char* fmt, ...) {
     char buf[512];
@@ -183,16 +181,7 @@ cudaError_t launch(vx_handle* h, void (*kern)(KArgs...), dim3 grid, dim3 block, 
   cfg.attrs = at;
   cfg.numAttrs = h->use_pdl ? 1 : 0;
   h->launches++;
-  if (!h->profiling) return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-  vx_handle::ProfEv ev{nullptr, nullptr, h->cur_cat};
-  cudaEventCreate(&ev.a);
-  cudaEventCreate(&ev.b);
-  cudaEventRecord(ev.a, h->stream);
-  cudaError_t r = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-  cudaEventRecord(ev.b, h->stream);
-  h->prof.push_back(ev);
-  h->cur_cat = 2;
-  return r;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 template <int M, int R, int CPL, int EPI, bool NORM>
@@ -235,9 +224,9 @@ int run_gemv(vx_handle* h, const gemv::Params& p) {
     // algorithmic bytes: the weight slice once, x once, y written (read too for residual adds)
     const double w = (double)p.rows * p.kc * 2.0 * (EPI == gemv::kSwiglu ? 2.0 : 1.0);
     const double xy = (double)M * p.kc * 4.0 + (double)M * p.rows * 4.0 * (EPI == gemv::kResid ? 2.0 : 1.0);
-    h->prof_bytes[0] += w + xy;
-    h->cur_cat = 0;
+    h->prof_bytes += w + xy;
   }
+  if (!(h->parts & 2)) return VX_OK;
   CK(launch(h, kern, dim3(grid), dim3(gemv::kThreads), gemv::kSmemBytes, p));
   return VX_OK;
 }
@@ -309,7 +298,7 @@ int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const 
   ep.slots = h->slots; ep.rows = h->rows_in; ep.prompt = h->prompt; ep.voice = h->voice;
   ep.max_seq = h->cfg.max_seq_len; ep.max_voice = h->cfg.max_voice_rows; ep.code_ring = h->code_ring;
   ep.h = h->h + (long long)slot * D; ep.D = D; ep.slot0 = slot;
-  CK(launch(h, k_embed, dim3(1), dim3(256), 0, ep));
+  if (h->parts & 1) CK(launch(h, k_embed, dim3(1), dim3(256), 0, ep));
   if (dbg && (rc = dbg_rows(h, ep.h, nullptr, dbg->base))) return rc;
 
   float* hs = h->h + (long long)slot * D;
@@ -335,7 +324,7 @@ int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const 
       ap.tickets = h->attn_tickets + (long long)slot * h->NKV;
       ap.kv = kg; ap.layer = l; ap.pos = &h->slots[0].pos; ap.pos_stride = kPosStride; ap.slot0 = slot;
       ap.n_splits = h->n_splits; ap.scale = 1.0f / sqrtf((float)h->HD);
-      h->cur_cat = 1;
+      if (h->parts & 4)
       CK(launch(h, attn::k_attn_decode, dim3(h->NKV, h->n_splits, 1), dim3(attn::kThreads), attn::kSmemBytes,
                 h->kv_map, ap));
     }
@@ -348,7 +337,7 @@ int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const 
       else if (h->QD == 512) rc = (h->rank == 0) ? run_gemv<1, 8, 1, gemv::kResid, false>(h, p) : run_gemv<1, 8, 1, gemv::kStore, false>(h, p);
       else rc = h->fail(VX_E_INVALID, "unsupported local q width %d", h->QD);
       if (rc) return rc;
-      if ((rc = allreduce_inplace(h, hs, D))) return rc;
+      if ((h->parts & 2) && (rc = allreduce_inplace(h, hs, D))) return rc;
     }
     if (dbg && (rc = dbg_rows(h, hs, nullptr, dbg->base + (size_t)(2 + 4 * l) * D))) return rc;
     if (dbg && (rc = dbg_rows(h, hs, W.ffn_norm, dbg->base + (size_t)(3 + 4 * l) * D))) return rc;
@@ -367,7 +356,7 @@ int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const 
       else if (h->Fl == 1152) rc = (h->rank == 0) ? run_gemv<1, 8, 2, gemv::kResid, false>(h, p) : run_gemv<1, 8, 2, gemv::kStore, false>(h, p);
       else rc = h->fail(VX_E_INVALID, "unsupported local FFN width %d", h->Fl);
       if (rc) return rc;
-      if ((rc = allreduce_inplace(h, hs, D))) return rc;
+      if ((h->parts & 2) && (rc = allreduce_inplace(h, hs, D))) return rc;
     }
     if (dbg && (rc = dbg_rows(h, hs, nullptr, dbg->base + (size_t)(4 + 4 * l) * D))) return rc;
   }
@@ -375,7 +364,7 @@ int enqueue_backbone(vx_handle* h, int slot, bool inc_frame, bool record, const 
   fp.h = hs; fp.w = h->final_norm; fp.out = h->normed + (long long)slot * D; fp.D = D; fp.eps = h->cfg.norm_eps;
   fp.slots = h->slots; fp.slot0 = slot; fp.inc_pos = 1; fp.inc_frame = inc_frame ? 1 : 0;
   fp.normed_ring = record ? h->normed_ring : nullptr;
-  CK(launch(h, k_final_norm, dim3(1), dim3(256), 0, fp));
+  if (h->parts & 1) CK(launch(h, k_final_norm, dim3(1), dim3(256), 0, fp));
   if (dbg) {
     if ((rc = dbg_rows(h, fp.out, nullptr, dbg->base + (size_t)(1 + 4 * h->L) * D))) return rc;
     if ((rc = dbg_rows(h, hs, nullptr, dbg->base + (size_t)(2 + 4 * h->L) * D))) return rc;
@@ -697,7 +686,7 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   h->max_pages = (c.max_seq_len + kPage - 1) / kPage;
   const long long total_pages = (long long)h->B * h->max_pages;
   h->kv_rows = total_pages * h->L * 2 * h->NKV * kPage;
-  h->n_splits = std::max(1, std::min(h->max_pages, (2 * h->num_sms + h->NKV - 1) / h->NKV));
+  h->n_splits = std::max(1, std::min(std::min(h->max_pages, attn::kMaxSplits), (2 * h->num_sms + h->NKV - 1) / h->NKV));
   size_t act = 0;
   auto f32n = [&](size_t n) { act += ((n * 4 + 255) & ~size_t(255)); };
   f32n(64);  // rope
@@ -1148,38 +1137,70 @@ int vx_rewind(vx_handle* h, int32_t slot) {
   return VX_OK;
 }
 
+// Capture one backbone step restricted to `parts` as a graph (not cached).
+static int capture_parts(vx_handle* h, int slot, int parts, cudaGraphExec_t* exec) {
+  cudaGraph_t graph;
+  h->parts = parts;
+  h->profiling = (parts == 2);
+  if (h->profiling) h->prof_bytes = 0;
+  const long long before = h->launches;
+  cudaError_t ce = cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal);
+  int rc = ce == cudaSuccess ? enqueue_backbone(h, slot, false, false, nullptr) : VX_E_CUDA;
+  cudaError_t ee = cudaStreamEndCapture(h->stream, &graph);
+  h->parts = 7;
+  h->profiling = false;
+  h->launches = before;
+  if (rc || ce != cudaSuccess || ee != cudaSuccess) {
+    if (ee == cudaSuccess) cudaGraphDestroy(graph);
+    return rc ? rc : h->fail(VX_E_CUDA, "profile capture failed");
+  }
+  cudaError_t ie = cudaGraphInstantiate(exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) return h->fail(VX_E_CUDA, "profile instantiate: %s", cudaGetErrorString(ie));
+  return VX_OK;
+}
+
 int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, double* out_bytes) {
   int rc = check_slot(h, slot);
   if (rc) return rc;
   if (!out_ms || reps < 1) return h->fail(VX_E_INVALID, "profile args");
   if ((rc = need_positions(h, slot, reps))) return rc;
   CK(cudaSetDevice(h->dev));
-  const bool pdl = h->use_pdl;
-  h->use_pdl = false;            // events must bracket exactly one kernel
-  h->profiling = true;
-  h->prof.clear();
-  h->prof_bytes[0] = h->prof_bytes[1] = h->prof_bytes[2] = 0;
-  for (int i = 0; i < reps && rc == VX_OK; ++i) {
-    rc = set_slot_fields(h, slot, kEmbSynthCodes, 0);
-    if (!rc) rc = enqueue_backbone(h, slot, false, false, nullptr);
-    if (!rc) h->pos_host[slot] += 1;
+  // the slot's decode state is saved and restored around the measurement
+  SlotState saved;
+  CK(cudaMemcpyAsync(&saved, &h->slots[slot], sizeof(SlotState), cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  if ((rc = set_slot_fields(h, slot, kEmbSynthCodes, 0))) return rc;
+  cudaGraphExec_t g[3] = {nullptr, nullptr, nullptr};
+  const int parts[3] = {7, 2, 4};
+  double gemv_bytes = 0;
+  for (int k = 0; k < 3 && !rc; ++k) {
+    rc = capture_parts(h, slot, parts[k], &g[k]);
+    if (parts[k] == 2) gemv_bytes = h->prof_bytes;
   }
-  h->profiling = false;
-  h->use_pdl = pdl;
-  cudaError_t se = cudaStreamSynchronize(h->stream);
-  float acc[3] = {0, 0, 0};
-  for (auto& ev : h->prof) {
-    float ms = 0.f;
-    if (se == cudaSuccess && cudaEventElapsedTime(&ms, ev.a, ev.b) == cudaSuccess) acc[ev.cat] += ms;
-    cudaEventDestroy(ev.a);
-    cudaEventDestroy(ev.b);
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (!rc) { cudaEventCreate(&a); cudaEventCreate(&b); }
+  for (int k = 0; k < 3 && !rc; ++k) {
+    // one untimed launch, then `reps` timed launches back to back
+    if (cudaGraphLaunch(g[k], h->stream) != cudaSuccess) { rc = h->fail(VX_E_CUDA, "profile launch"); break; }
+    cudaEventRecord(a, h->stream);
+    for (int i = 0; i < reps; ++i) cudaGraphLaunch(g[k], h->stream);
+    cudaEventRecord(b, h->stream);
+    if (cudaEventSynchronize(b) != cudaSuccess) { rc = h->fail(VX_E_CUDA, "profile sync"); break; }
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    out_ms[k] = ms / reps;
+    // restore the position advanced by the full-step graph
+    CK(cudaMemcpyAsync(&h->slots[slot], &saved, sizeof(SlotState), cudaMemcpyHostToDevice, h->stream));
+    if ((rc = set_slot_fields(h, slot, kEmbSynthCodes, 0))) break;
   }
-  h->prof.clear();
+  for (auto& x : g) if (x) cudaGraphExecDestroy(x);
+  if (a) cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  CK(cudaMemcpyAsync(&h->slots[slot], &saved, sizeof(SlotState), cudaMemcpyHostToDevice, h->stream));
   if (rc) return rc;
-  if (se != cudaSuccess) return h->fail(VX_E_CUDA, "profile: %s", cudaGetErrorString(se));
-  for (int k = 0; k < 3; ++k) out_ms[k] = acc[k] / reps;
-  if (out_bytes) out_bytes[0] = h->prof_bytes[0] / reps;
-  return check_device_error(h);
+  if (out_bytes) out_bytes[0] = gemv_bytes;
+  return finish(h);
 }
 
 int vx_nccl_unique_id(const char* lib, uint8_t out[128]) {

@@ -257,12 +257,12 @@ class VoxtralEngine:
     def rewind(self, slot: int = 0):
         self._check(load_library().vx_rewind(self._h, slot))
 
-    def profile_step(self, reps: int = 4, slot: int = 0) -> dict:
-        """Per-category kernel time of one backbone step (CUDA events around each launch)."""
+    def profile_step(self, reps: int = 8, slot: int = 0) -> dict:
+        """ms per backbone step of the full graph, its GEMV chain and its attention chain."""
         ms = np.zeros(3, np.float32)
         by = ctypes.c_double()
         self._check(load_library().vx_profile_step(self._h, slot, reps, _p(ms, _f32p), ctypes.byref(by)))
-        return {"gemv_ms": float(ms[0]), "attn_ms": float(ms[1]), "other_ms": float(ms[2]),
+        return {"step_ms": float(ms[0]), "gemv_ms": float(ms[1]), "attn_ms": float(ms[2]),
                 "gemv_bytes": float(by.value)}
 
     # ------------------------------------------------------------------ steps
