@@ -154,8 +154,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const __grid_constant__ Pa
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       const uint32_t rowbytes = (uint32_t)p.kc * 2u;
+      // L2 prefetch of the tiles kAhead iterations ahead keeps DRAM busy beyond the ring
+      constexpr int kAhead = 8;
+      auto prefetch_tile = [&](int tt) {
+        const int r0 = tt * ORT;
+        const int nr = min(ORT, p.rows - r0);
+        const __half* src = p.W + (long long)r0 * p.ldw + p.col0;
+        if (p.kc == p.ldw) {
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"((uint32_t)nr * rowbytes) : "memory");
+          if (EPI == kSwiglu)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src + p.second_off),
+                         "r"((uint32_t)nr * rowbytes) : "memory");
+        }
+      };
+      for (int k = 0; k < kAhead; ++k)
+        if (blockIdx.x + k * (int)gridDim.x < ntiles) prefetch_tile(blockIdx.x + k * gridDim.x);
       int it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+        if (t + kAhead * (int)gridDim.x < ntiles) prefetch_tile(t + kAhead * gridDim.x);
         const int s = it % kStages;
         const uint32_t ph = (uint32_t)(it / kStages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, kDevTimeoutEmpty)) break;

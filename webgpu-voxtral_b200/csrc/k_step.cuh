@@ -1,0 +1,836 @@
+// k_step.cuh — persistent decode megakernel: many backbone steps in one launch.
+//
+// Replaces the reference's per-token command stream (backboneStep, src/engine.ts:814-1042:
+// ~450 dispatches per token, one queue.submit per token in the prefill loop :2457-2472
+// and per frame in the decode loop :2498-2541) with ONE cooperative launch that runs
+// `n_frames` consecutive backbone steps of one utterance.
+//
+// Each step is a fixed program of phases separated by grid-wide barriers:
+//   EMBED | 26 x ( QKV+RoPE+KV-append | ATTENTION | O+residual | W13+SwiGLU | W2+residual ) | FINAL-NORM
+// Grid: one CTA per SM, 10 warps.
+//   warp 0  producer: walks every GEMV phase of every step and streams the weight
+//           tiles assigned to this CTA through a 4-stage ring (TMA bulk copies).
+//           Weights never depend on activations, so it never waits on a barrier:
+//           while the consumers wait at a phase boundary the ring keeps filling,
+//           and HBM stays busy across all phases, layers and steps.
+//   warps 1-8 consumers: GEMV partial sums from the ring (x' slice in registers),
+//           attention (mma.sync over TMA-loaded f16 KV pages), embedding and final
+//           norm slices.
+//   warp 9  epilogue: per-tile sums, fused epilogue (RoPE + KV append, residual,
+//           SwiGLU), and this CTA's arrival at the grid barrier of each GEMV phase.
+// Tiles of GEMV phase p are dealt round-robin starting at CTA (sum of earlier tile
+// counts) mod G, so every CTA's cumulative share of the weight stream stays within
+// one tile of the others.
+// Every wait is bounded (vx_common.cuh): an expired wait records a device error and
+// the kernel unwinds instead of hanging.
+#pragma once
+#include "k_attn.cuh"
+#include "k_gemv.cuh"
+#include "k_misc.cuh"
+
+namespace vx {
+namespace mk {
+
+constexpr int kCW = 8;
+constexpr int kThreads = (kCW + 2) * 32;
+constexpr int kStages = 4;
+constexpr int kStageBytes = 36864;
+constexpr int kRedSlots = 4;
+constexpr int kMaxVals = 32;
+constexpr int D = 3072, QD = 4096, KVD = 1024, QKVD = 6144, F = 9216, HD = 128, NKV = 8, GQA = 4;
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr int kOffRing = 0;
+constexpr int kOffAttn = kStages * kStageBytes;            // 147456, 1024-aligned
+constexpr int kAttnBytes = 65536;                          // a pair of K/V pages
+constexpr int kOffBars = kOffAttn + kAttnBytes;            // mbarriers
+constexpr int kOffRed = kOffBars + 256;
+constexpr int kOffScratch = kOffRed + kRedSlots * kCW * kMaxVals * 4;
+constexpr int kScratchBytes = 4096;   // [0,256) combine weights / norm partials, [768,805) codes
+constexpr size_t kSmemBytes = (size_t)kOffScratch + kScratchBytes + 1024;   // + alignment slack
+
+// tiles per GEMV phase (rows per tile: QKV 6, O 4, W13 3 outputs, W2 2)
+constexpr int kTilesQKV = QKVD / 6, kTilesO = D / 4, kTilesW13 = F / 3, kTilesW2 = D / 2;
+constexpr int kTilesLayer = kTilesQKV + kTilesO + kTilesW13 + kTilesW2;
+
+struct LayerPtrs {
+  const __half *wqkv, *wo, *w13, *w2, *attn_norm, *ffn_norm;
+};
+
+struct StepParams {
+  const LayerPtrs* layers;
+  int n_layers;
+  const __half* tok; int vocab;
+  const __half* audio; int audio_rows;
+  const float* rows_in;
+  const int32_t* prompt; const float* voice; int max_seq, max_voice;
+  uint32_t* code_ring;
+  float *h, *q, *att, *g, *normed, *normed_ring;
+  const __half* final_norm;
+  float eps;
+  gemv::KvGeom kv;
+  float* part; int* tickets; int n_splits;
+  const float* rope_freq;
+  SlotState* slots; int slot;
+  unsigned* bar;          // grid barrier counter, zero at launch
+  unsigned long long* trace;  // nullable: [G][kTraceFrames * phases][3] globaltimer stamps
+  int prefetch_ahead;     // weight tiles prefetched into L2 ahead of the ring (0..kMaxPrefetchAhead)
+  int prestage_kv;        // stage the first K/V page pair of each attention item during QKV
+  int n_frames;
+  int mode0, token0;      // embedding of the first step
+  int mode_next;          // embedding of later steps
+  int inc_frame, record;  // advance the frame counter / record normed states per step
+};
+
+struct Smem {
+  uint8_t* ring;
+  uint8_t* attn;
+  uint64_t *full, *empty, *rfull, *rempty, *afull;
+  float* red;
+  float* scratch;
+};
+
+__device__ __forceinline__ Smem smem_map(uint8_t* raw) {
+  uint8_t* b = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  Smem s;
+  s.ring = b + kOffRing;
+  s.attn = b + kOffAttn;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b + kOffBars);
+  s.full = bars; s.empty = bars + kStages; s.rfull = bars + 2 * kStages; s.rempty = s.rfull + kRedSlots;
+  s.afull = s.rempty + kRedSlots;
+  s.red = reinterpret_cast<float*>(b + kOffRed);
+  s.scratch = reinterpret_cast<float*>(b + kOffScratch);
+  return s;
+}
+
+// ---------------------------------------------------------------- grid barrier
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Consumers (256 threads) wait until `target` CTA-phase arrivals are counted.  One
+// thread polls (relaxed loads, then one acquire fence); the named barrier releases
+// the others.  Writers publish with bar.sync + one red.release (no full fence).
+__device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid) {
+  if (ctid == 0) {
+    uint32_t i = 0;
+    while (ld_relaxed(p.bar) < target) {
+      if (++i > (1u << 27) || ((i & 1023u) == 0 && error_set())) {
+        if (i > (1u << 27)) set_error(kDevTimeoutRed);
+        break;
+      }
+    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  }
+  named_bar_sync(1, kCW * 32);
+}
+// Arrival of this CTA for the current phase, by the warp that wrote its outputs.
+__device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, bool kv_written) {
+  if (kv_written) fence_proxy_async_global();   // KV rows (st.global) are read by TMA next phase
+  __syncwarp();
+  if (lane == 0) red_release_add(p.bar, 1u);
+}
+// Phase trace (globaltimer ns) for the first kTraceFrames steps when p.trace is set:
+// [cta][phase][0] = consumers released, [1] = consumers done, [2] = epilogue arrival.
+constexpr int kTraceFrames = 2;
+__device__ __forceinline__ void trace_mark(const StepParams& p, int c, int f, int kl, int which, int L, int t0) {
+  if (p.trace && f < kTraceFrames && t0 == 0)
+    p.trace[(((long long)c * kTraceFrames + f) * (2 + 5 * L) + kl) * 3 + which] = globaltimer();
+}
+
+__device__ __forceinline__ int first_tile(int c, int off, int G) { return (c - off % G + G) % G; }
+
+// ---------------------------------------------------------------- producer
+// Position in this CTA's sequence of weight tiles: (frame, layer, GEMV kind, tile).
+constexpr int kMaxPrefetchAhead = 32;   // bound on StepParams::prefetch_ahead
+__device__ __constant__ int kTilesOf[4] = {kTilesQKV, kTilesO, kTilesW13, kTilesW2};
+__device__ __constant__ int kTilePrefix[4] = {0, kTilesQKV, kTilesQKV + kTilesO, kTilesQKV + kTilesO + kTilesW13};
+struct Cursor {
+  int f, l, k, t;
+  long long tb;   // tiles of all earlier layers (sets the dealing offset)
+};
+__device__ __forceinline__ void cursor_fix(Cursor& x, int c, int G, int L) {
+  while (x.t >= kTilesOf[x.k]) {
+    if (++x.k == 4) {
+      x.k = 0;
+      x.tb += kTilesLayer;
+      if (++x.l == L) { x.l = 0; ++x.f; }
+    }
+    x.t = first_tile(c, (int)((x.tb + kTilePrefix[x.k]) % G), G);
+  }
+}
+__device__ __forceinline__ void cursor_start(Cursor& x, int c, int G, int L) {
+  x.f = 0; x.l = 0; x.k = 0; x.tb = 0; x.t = first_tile(c, 0, G);
+  cursor_fix(x, c, G, L);
+}
+__device__ __forceinline__ void cursor_next(Cursor& x, int c, int G, int L) {
+  x.t += G;
+  cursor_fix(x, c, G, L);
+}
+// Source of a tile: first chunk (and the SwiGLU "up" chunk), bytes per chunk.
+__device__ __forceinline__ void tile_src(const StepParams& p, const Cursor& x, const __half*& a, const __half*& b,
+                                         uint32_t& bytes, int& ort) {
+  const LayerPtrs& W = p.layers[x.l];
+  b = nullptr;
+  switch (x.k) {
+    case 0: ort = 6; a = W.wqkv + (long long)x.t * 6 * D; bytes = min(6, QKVD - x.t * 6) * D * 2; break;
+    case 1: ort = 4; a = W.wo + (long long)x.t * 4 * QD; bytes = min(4, D - x.t * 4) * QD * 2; break;
+    case 2: ort = 3; a = W.w13 + (long long)x.t * 3 * D; b = a + (long long)F * D; bytes = min(3, F - x.t * 3) * D * 2; break;
+    default: ort = 2; a = W.w2 + (long long)x.t * 2 * F; bytes = min(2, D - x.t * 2) * F * 2; break;
+  }
+}
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------- consumer GEMV phase
+template <int R, int CPL, bool NORM>
+__device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& it, uint32_t& rit, const float* x,
+                                       const __half* norm_w, int kc, int T, int off, int c, int G, int cw, int lane) {
+  constexpr int P = gemv::Pow2<R>::v;
+  // x' slice in registers.  For the RMSNorm variants each warp's slice (CPL x 128
+  // columns; the 8 slices partition the row) also gives its partial sum of squares,
+  // so the norm costs one load round and one named barrier.
+  float xr[CPL][4];
+  float2 wn[CPL][2];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int col = (cw + kCW * j) * 128 + lane * 4;
+    const float4 v = *reinterpret_cast<const float4*>(x + col);
+    xr[j][0] = v.x; xr[j][1] = v.y; xr[j][2] = v.z; xr[j][3] = v.w;
+    if (NORM) {
+      const __half2* w2 = reinterpret_cast<const __half2*>(norm_w + col);
+      wn[j][0] = __half22float2(w2[0]);
+      wn[j][1] = __half22float2(w2[1]);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  }
+  if (NORM) {
+    ss = warp_sum(ss);
+    if (lane == 0) s.scratch[cw] = ss;
+    named_bar_sync(1, kCW * 32);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) tot += s.scratch[w];
+    const float rms = 1.0f / sqrtf(tot / (float)(CPL * kCW * 128) + p.eps);
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      xr[j][0] = xr[j][0] * rms * wn[j][0].x; xr[j][1] = xr[j][1] * rms * wn[j][0].y;
+      xr[j][2] = xr[j][2] * rms * wn[j][1].x; xr[j][3] = xr[j][3] * rms * wn[j][1].y;
+    }
+  }
+  const int my_idx = gemv::transpose_index<P>(lane);
+  const bool writer = lane < P && my_idx < R;
+  const uint32_t rowbytes = (uint32_t)kc * 2u;
+  for (int t = first_tile(c, off, G); t < T; t += G, ++it, ++rit) {
+    const int st = it % kStages;
+    if (!mbar_wait(&s.full[st], (it / kStages) & 1u, kDevTimeoutFull)) return false;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    const uint8_t* base = s.ring + (size_t)st * kStageBytes + (size_t)(cw * 128 + lane * 4) * 2;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const uint2 wv = *reinterpret_cast<const uint2*>(base + (size_t)r * rowbytes + (size_t)j * kCW * 256);
+        const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+        const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+        float a = acc[r];
+        a = fmaf(w01.x, xr[j][0], a);
+        a = fmaf(w01.y, xr[j][1], a);
+        a = fmaf(w23.x, xr[j][2], a);
+        a = fmaf(w23.y, xr[j][3], a);
+        acc[r] = a;
+      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.empty[st]);
+    float v[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) v[i] = i < R ? acc[i] : 0.f;
+    const float rv = gemv::transpose_reduce<P>(v, lane);
+    const int rs = rit % kRedSlots;
+    if (!mbar_wait(&s.rempty[rs], ((rit / kRedSlots) & 1u) ^ 1u, kDevTimeoutRed)) return false;
+    if (writer) s.red[(rs * kCW + cw) * kMaxVals + my_idx] = rv;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.rfull[rs]);
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- epilogue GEMV phase
+// EPI: gemv::kQkv (rows -> q / K / V with RoPE), kResid (y += ), kSwiglu (g = silu(a)*b)
+template <int R, int EPI>
+__device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t& rit, float* y, int rows, int T,
+                                         int off, int c, int G, int lane, int layer, int pos) {
+  constexpr int ORT = EPI == gemv::kSwiglu ? R / 2 : R;
+  for (int t = first_tile(c, off, G); t < T; t += G, ++rit) {
+    const int rs = rit % kRedSlots;
+    float yold = 0.f;   // residual row loaded before the wait so its latency overlaps it
+    if constexpr (EPI == gemv::kResid) {
+      const int row = t * ORT + lane;
+      if (lane < R && row < rows) yold = y[row];
+    }
+    if (!mbar_wait(&s.rfull[rs], (rit / kRedSlots) & 1u, kDevTimeoutRed)) return false;
+    float val = 0.f;
+    if (lane < R) {
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) val += s.red[(rs * kCW + w) * kMaxVals + lane];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.rempty[rs]);
+    const int r = lane;
+    if constexpr (EPI == gemv::kResid) {
+      const int row = t * ORT + r;
+      if (r < R && row < rows) y[row] = yold + val;
+    } else if constexpr (EPI == gemv::kSwiglu) {
+      const float up = __shfl_down_sync(0xffffffffu, val, ORT);
+      const int row = t * ORT + r;
+      if (r < ORT && row < rows) y[row] = swiglu(val, up);
+    } else {
+      const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+      const int row = t * R + r;
+      if (r < R && row < rows) {
+        float out = val;
+        if (row < QD + KVD) {
+          const float ang = (float)pos * p.rope_freq[(row & 127) >> 1];
+          float sn, cs;
+          sincosf(ang, &sn, &cs);
+          const bool even = (row & 1) == 0;
+          const float x0 = even ? val : other, x1 = even ? other : val;
+          out = even ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        }
+        if (row < QD) {
+          p.q[row] = out;
+        } else {
+          const int kvr = row - QD;
+          const int kv = kvr >= KVD ? 1 : 0;
+          const int rr = kvr - kv * KVD;
+          const int lp = pos / p.kv.page_size;
+          if (lp >= p.kv.max_pages) {
+            set_error(kDevBadIndex);
+          } else {
+            const int page = p.kv.page_table[(long long)p.slot * p.kv.max_pages + lp];
+            const long long prow = gemv::kv_row(p.kv, page, layer, kv, rr >> 7, pos % p.kv.page_size);
+            p.kv.pool[prow * HD + (rr & 127)] = __float2half_rn(out);
+          }
+        }
+      }
+    }
+  }
+  grid_arrive_warp(p, lane, EPI == gemv::kQkv);
+  return true;
+}
+
+// ---------------------------------------------------------------- attention phase
+// Split-KV flash decode over the pages of (kv head, split) items dealt to this CTA.
+// 8 warps: warps 0-3 take page 2i of a pair, warps 4-7 page 2i+1, 16 positions each.
+// TMA of K/V pages [pp, pp+npair) of one KV head into the attention buffer (thread 0).
+__device__ __forceinline__ void issue_pair(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int kvh,
+                                           int pp, int npair) {
+  const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
+  mbar_arrive_expect_tx(s.afull, (uint32_t)npair * 32768u);
+  for (int k = 0; k < npair; ++k) {
+    const int phys = ptab[pp + k];
+    const int krow = (int)gemv::kv_row(p.kv, phys, layer, 0, kvh, 0);
+    const int vrow = (int)gemv::kv_row(p.kv, phys, layer, 1, kvh, 0);
+    uint8_t* dst = s.attn + k * 32768;
+    tma_load_2d(dst, kvmap, 0, krow, s.afull);
+    tma_load_2d(dst + 8192, kvmap, 64, krow, s.afull);
+    tma_load_2d(dst + 16384, kvmap, 0, vrow, s.afull);
+    tma_load_2d(dst + 24576, kvmap, 64, vrow, s.afull);
+  }
+}
+// Called at the start of the QKV phase: the first page pair of this CTA's attention
+// item holds only positions written by earlier steps (except the current position's
+// row, patched in the attention phase), so its TMA can run under the QKV phase.
+__device__ __forceinline__ bool prestage(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int pos,
+                                         int c, int ctid, bool& a_pending) {
+  if (!p.prestage_kv || c >= NKV * p.n_splits) return false;
+  const int npages = (pos + 1 + 63) / 64;
+  const int pps = (npages + p.n_splits - 1) / p.n_splits;
+  const int kvh = c / p.n_splits, split = c % p.n_splits;
+  const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
+  if (pg0 >= pg1) return false;
+  if (ctid == 0 && !error_set()) {
+    a_pending = true;
+    issue_pair(p, kvmap, s, layer, kvh, pg0, min(2, pg1 - pg0));
+  }
+  return true;
+}
+
+// Control flow is uniform across the 256 consumer threads (every named barrier is
+// reached by all of them); after a device error the work is skipped, not the barriers.
+__device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap* kvmap, Smem& s, uint32_t& ait,
+                                          bool& a_pending, bool staged, int layer, int pos, int c, int G, int cw,
+                                          int lane, int ctid) {
+  const int seq = pos + 1;
+  const int npages = (seq + 63) / 64;
+  const int pps = (npages + p.n_splits - 1) / p.n_splits;
+  const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
+  const float scale = 0.08838834764831845f;   // 1/sqrt(128) rounded to f32
+  const int g = lane >> 2, hq = g & 3;
+  const bool lo_part = g >= 4;
+  const int half_pair = cw >> 2, grp = cw & 3;
+  __shared__ int s_last;
+  for (int item = c; item < NKV * p.n_splits; item += G) {
+    const int kvh = item / p.n_splits, split = item % p.n_splits;
+    const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
+    float m_run = -INFINITY, l_run = 0.f;
+    float o[16][4];
+    uint32_t qa0[8], qa2[8];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    for (int pp = pg0; pp < pg1; pp += 2) {
+      const int npair = min(2, pg1 - pp);
+      const bool go = !error_set();
+      const bool pre = staged && item == c && pp == pg0;   // already in flight since the QKV phase
+      if (ctid == 0 && go && !pre) {
+        a_pending = true;
+        issue_pair(p, kvmap, s, layer, kvh, pp, npair);
+      }
+      if (pp == pg0) {
+      // q fragments (hi rows 0-3, lo rows 4-7) for the 4 heads of this KV head, loaded
+      // while the first K/V pair is in flight
+      const float* qh = p.q + (long long)(kvh * GQA + hq) * HD;
+  #pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int cc = kk * 16 + (lane & 3) * 2;
+        float v0 = qh[cc], v1 = qh[cc + 1], v8 = qh[cc + 8], v9 = qh[cc + 9];
+        if (lo_part) {
+          v0 -= __half2float(__float2half_rn(v0)); v1 -= __half2float(__float2half_rn(v1));
+          v8 -= __half2float(__float2half_rn(v8)); v9 -= __half2float(__float2half_rn(v9));
+        }
+        qa0[kk] = pack_half2(v0, v1);
+        qa2[kk] = pack_half2(v8, v9);
+      }
+      }
+      const bool w_ok = go && mbar_wait(s.afull, ait & 1u, kDevTimeoutFull);
+      if (w_ok && ctid == 0) a_pending = false;
+      ++ait;
+      if (pre) {
+        // the current position's K/V row was written during the QKV phase: patch it
+        const int cp = pos / 64 - pp;
+        if (cp >= 0 && cp < npair) {
+          named_bar_sync(1, kCW * 32);
+          if (ctid < 32 && w_ok) {
+            const int kv = ctid >> 4, ch = ctid & 15, r = pos & 63;
+            const int phys = ptab[pp + cp];
+            const uint4 v = *reinterpret_cast<const uint4*>(
+                p.kv.pool + gemv::kv_row(p.kv, phys, layer, kv, kvh, r) * HD + ch * 8);
+            *reinterpret_cast<uint4*>(s.attn + cp * 32768 + kv * 16384 + (ch >> 3) * 8192 + r * 128 +
+                                      (((ch & 7) ^ (r & 7)) << 4)) = v;
+          }
+          named_bar_sync(1, kCW * 32);
+        }
+      }
+      if (w_ok && half_pair < npair) {
+        const int pg = pp + half_pair;
+        const uint32_t kbase = smem_u32(s.attn + half_pair * 32768);
+        const uint32_t vbase = kbase + 16384;
+        float sacc[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+        const int mat = lane >> 3, r8 = lane & 7;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(b0, b1, b2, b3, kbase + attn::swz(grp * 16 + (mat >> 1) * 8 + r8, kk * 16 + (mat & 1) * 8));
+          mma_16816(sacc[0], qa0[kk], 0u, qa2[kk], 0u, b0, b1);
+          mma_16816(sacc[1], qa0[kk], 0u, qa2[kk], 0u, b2, b3);
+        }
+        float sc[2][2], mloc = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float fd = sacc[j][e] + __shfl_xor_sync(0xffffffffu, sacc[j][e], 16);
+            const int ppos = pg * 64 + grp * 16 + j * 8 + (lane & 3) * 2 + e;
+            sc[j][e] = ppos < seq ? fd * scale : -INFINITY;
+            mloc = fmaxf(mloc, sc[j][e]);
+          }
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+        const float m_new = fmaxf(m_run, mloc);
+        const float corr = (m_new == -INFINITY) ? 1.f : expf(m_run - m_new);
+        float psum = 0.f, pv[2][2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float pe = sc[j][e] == -INFINITY ? 0.f : expf(sc[j][e] - m_new);
+            psum += pe;
+            pv[j][e] = lo_part ? pe - __half2float(__float2half_rn(pe)) : pe;
+          }
+        const uint32_t pa0 = pack_half2(pv[0][0], pv[0][1]), pa2 = pack_half2(pv[1][0], pv[1][1]);
+        l_run = l_run * corr + psum;
+        m_run = m_new;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { o[j][0] *= corr; o[j][1] *= corr; }
+#pragma unroll
+        for (int dt2 = 0; dt2 < 8; ++dt2) {
+          uint32_t v0, v1, v2, v3;
+          ldmatrix_x4_trans(v0, v1, v2, v3, vbase + attn::swz(grp * 16 + (mat & 1) * 8 + r8, dt2 * 16 + (mat >> 1) * 8));
+          mma_16816(o[2 * dt2], pa0, 0u, pa2, 0u, v0, v1);
+          mma_16816(o[2 * dt2 + 1], pa0, 0u, pa2, 0u, v2, v3);
+        }
+      }
+      named_bar_sync(1, kCW * 32);   // the pair buffer is free again
+    }
+    // merge the 8 warps (reuse the pair buffer as scratch)
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] += __shfl_xor_sync(0xffffffffu, o[j][0], 16);
+      o[j][1] += __shfl_xor_sync(0xffffffffu, o[j][1], 16);
+    }
+    float* ws = reinterpret_cast<float*>(s.attn);     // [8 warps][4 heads][130]
+    if (lane < 16) {
+      float* w = ws + (cw * GQA + hq) * attn::kPartStride;
+      if ((lane & 3) == 0) { w[0] = m_run; w[1] = l_run; }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int d = j * 8 + (lane & 3) * 2;
+        w[2 + d] = o[j][0];
+        w[3 + d] = o[j][1];
+      }
+    }
+    named_bar_sync(1, kCW * 32);
+    float* part = p.part + ((long long)kvh * p.n_splits + split) * (GQA * attn::kPartStride);
+    for (int idx = ctid; idx < GQA * HD; idx += kCW * 32) {
+      const int h = idx / HD, d = idx % HD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) M = fmaxf(M, ws[(w * GQA + h) * attn::kPartStride]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) {
+          const float* ww = ws + (w * GQA + h) * attn::kPartStride;
+          const float f = ww[0] == -INFINITY ? 0.f : expf(ww[0] - M);
+          L += ww[1] * f;
+          O += ww[2 + d] * f;
+        }
+      }
+      part[h * attn::kPartStride + 2 + d] = O;
+      if (d == 0) { part[h * attn::kPartStride] = M; part[h * attn::kPartStride + 1] = L; }
+    }
+    named_bar_sync(1, kCW * 32);
+    if (ctid == 0) s_last = (atom_add_acq_rel(&p.tickets[kvh], 1) == p.n_splits - 1);
+    named_bar_sync(1, kCW * 32);
+    if (s_last) {
+      const float* pb = p.part + (long long)kvh * p.n_splits * (GQA * attn::kPartStride);
+      const int n_used = min(p.n_splits, (npages + pps - 1) / pps);
+      float* sw = s.scratch;                            // [64 splits][4 heads]
+      if (cw < GQA) {
+        const int h = cw;
+        float ms[2], ls[2], M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int sp = lane + 32 * j;
+          ms[j] = sp < n_used ? __ldcg(pb + sp * GQA * attn::kPartStride + h * attn::kPartStride) : -INFINITY;
+          ls[j] = sp < n_used ? __ldcg(pb + sp * GQA * attn::kPartStride + h * attn::kPartStride + 1) : 0.f;
+          M = fmaxf(M, ms[j]);
+        }
+        M = warp_max(M);
+        float f[2], L = 0.f;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) { f[j] = ms[j] == -INFINITY ? 0.f : expf(ms[j] - M); L += ls[j] * f[j]; }
+        L = warp_sum(L);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          if (lane + 32 * j < n_used) sw[(lane + 32 * j) * GQA + h] = f[j] / L;
+      }
+      named_bar_sync(1, kCW * 32);
+      for (int idx = ctid; idx < GQA * HD; idx += kCW * 32) {
+        const int h = idx / HD, d = idx % HD;
+        float O = 0.f;
+#pragma unroll 8
+        for (int sp = 0; sp < n_used; ++sp) O += __ldcg(pb + sp * GQA * attn::kPartStride + h * attn::kPartStride + 2 + d) * sw[sp * GQA + h];
+        p.att[(kvh * GQA + h) * HD + d] = O;
+      }
+      if (ctid == 0) p.tickets[kvh] = 0;
+    }
+    named_bar_sync(1, kCW * 32);
+  }
+}
+
+// ---------------------------------------------------------------- embedding / final norm slices
+__device__ __forceinline__ int embed_source(const StepParams& p, int mode, int token, int pos, int frame,
+                                            uint32_t* codes, int& row) {
+  SlotState& st = p.slots[p.slot];
+  switch (mode) {
+    case kEmbToken: row = token; return (row >= 0 && row < p.vocab) ? 0 : -1;
+    case kEmbAudioToken: row = token; return (row >= 0 && row < p.audio_rows) ? 1 : -1;
+    case kEmbRow: return 2;
+    case kEmbCodes:
+      for (int k = 0; k < 37; ++k) codes[k] = st.codes[k];
+      break;
+    case kEmbSynthCodes: {
+      const uint64_t base = 37ull * (uint64_t)(frame - 1);
+      codes[0] = 2u + (uint32_t)(vx_bits(st.codes_key, base) % 8192ull);
+      for (int k = 0; k < kNumAc; ++k) codes[1 + k] = 2u + (uint32_t)(vx_bits(st.codes_key, base + 1 + k) % 21ull);
+      break;
+    }
+    case kEmbPrompt: {
+      if (pos < 0 || pos >= p.max_seq || pos >= st.prompt_len) return -1;
+      const int t = p.prompt[(long long)p.slot * p.max_seq + pos];
+      if (t < 0) { row = -t - 1; return row < p.max_voice ? 4 : -1; }
+      row = t;
+      return row < p.vocab ? 0 : -1;
+    }
+    default: return -1;
+  }
+  bool ok = codes[0] < (uint32_t)p.audio_rows;
+  for (int k = 0; k < kNumAc; ++k) ok = ok && (kAcBase + kAcStride * k + (int)codes[1 + k] < p.audio_rows);
+  return ok ? 3 : -1;
+}
+
+// ---------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_constant__ CUtensorMap kvmap,
+                                                              const __grid_constant__ StepParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem s = smem_map(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x, G = gridDim.x;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], kCW); }
+    for (int i = 0; i < kRedSlots; ++i) { mbar_init(&s.rfull[i], kCW); mbar_init(&s.rempty[i], 1); }
+    mbar_init(s.afull, 1);
+    fence_mbar_init();
+    prefetch_tmap(&kvmap);
+  }
+  __syncthreads();
+  const int pos0 = p.slots[p.slot].pos;
+  const int frame0 = p.slots[p.slot].frame;
+  const int L = p.n_layers;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      uint32_t it = 0;
+      Cursor cur, ahead;
+      cursor_start(cur, c, G, L);
+      cursor_start(ahead, c, G, L);
+      for (int i = 0; i < p.prefetch_ahead && ahead.f < p.n_frames; ++i) {
+        const __half *a, *b; uint32_t bytes; int ort;
+        tile_src(p, ahead, a, b, bytes, ort);
+        prefetch_l2(a, bytes);
+        if (b) prefetch_l2(b, bytes);
+        cursor_next(ahead, c, G, L);
+      }
+      while (cur.f < p.n_frames) {
+        const int st = it % kStages;
+        if (!mbar_wait(&s.empty[st], ((it / kStages) & 1u) ^ 1u, kDevTimeoutEmpty)) break;
+        const __half *a, *b; uint32_t bytes; int ort;
+        tile_src(p, cur, a, b, bytes, ort);
+        mbar_arrive_expect_tx(&s.full[st], bytes * (b ? 2u : 1u));
+        uint8_t* dst = s.ring + (size_t)st * kStageBytes;
+        bulk_g2s(dst, a, bytes, &s.full[st], pol);
+        if (b) bulk_g2s(dst + (size_t)ort * D * 2, b, bytes, &s.full[st], pol);   // SwiGLU up rows after the gate rows
+        ++it;
+        cursor_next(cur, c, G, L);
+        if (p.prefetch_ahead > 0 && ahead.f < p.n_frames) {
+          tile_src(p, ahead, a, b, bytes, ort);
+          prefetch_l2(a, bytes);
+          if (b) prefetch_l2(b, bytes);
+          cursor_next(ahead, c, G, L);
+        }
+      }
+      // drain the copies still in flight
+      const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0u;
+      for (uint32_t i = first; i < it; ++i)
+        if (!mbar_wait(&s.full[i % kStages], (i / kStages) & 1u, kDevTimeoutDrain)) break;
+    }
+    return;
+  }
+
+  uint32_t rit = 0;
+  if (warp == kCW + 1) {
+    // ------------------------------------------------------------ epilogue warp
+    long long tiles_before = 0;
+    for (int f = 0; f < p.n_frames; ++f) {
+      const int pos = pos0 + f;
+      for (int l = 0; l < L; ++l) {
+        const int o0 = (int)(tiles_before % G);
+        const int o1 = (int)((tiles_before + kTilesQKV) % G);
+        const int o2 = (int)((tiles_before + kTilesQKV + kTilesO) % G);
+        const int o3 = (int)((tiles_before + kTilesQKV + kTilesO + kTilesW13) % G);
+        const int kl = 1 + 5 * l;
+        if (!epilogue<6, gemv::kQkv>(p, s, rit, nullptr, QKVD, kTilesQKV, o0, c, G, lane, l, pos)) return;
+        trace_mark(p, c, f, kl, 2, L, lane);
+        if (!epilogue<4, gemv::kResid>(p, s, rit, p.h, D, kTilesO, o1, c, G, lane, l, pos)) return;
+        trace_mark(p, c, f, kl + 2, 2, L, lane);
+        if (!epilogue<6, gemv::kSwiglu>(p, s, rit, p.g, F, kTilesW13, o2, c, G, lane, l, pos)) return;
+        trace_mark(p, c, f, kl + 3, 2, L, lane);
+        if (!epilogue<2, gemv::kResid>(p, s, rit, p.h, D, kTilesW2, o3, c, G, lane, l, pos)) return;
+        trace_mark(p, c, f, kl + 4, 2, L, lane);
+        tiles_before += kTilesLayer;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers (warps 1-8)
+  const int cw = warp - 1, ctid = threadIdx.x - 32;
+  uint32_t it = 0, ait = 0;
+  unsigned phase = 0;                     // CTA-phase arrivals required before the next phase
+  long long tiles_before = 0;
+  const int per = (D + G - 1) / G;        // embedding / norm slice of this CTA
+  const int e0 = c * per, e1 = min(D, e0 + per);
+  uint32_t* codes = reinterpret_cast<uint32_t*>(s.scratch + 768);
+  bool a_pending = false;   // an attention TMA pair is in flight (thread 0)
+  for (int f = 0; f < p.n_frames; ++f) {
+    const int pos = pos0 + f, frame = frame0 + f;
+    // ---- EMBED
+    grid_wait(p, phase * G, ctid);
+    trace_mark(p, c, f, 0, 0, L, ctid);
+    {
+      int row = 0, kind = -1;
+      __shared__ int s_kind, s_row;
+      if (ctid == 0) {
+        kind = embed_source(p, f == 0 ? p.mode0 : p.mode_next, p.token0, pos, frame, codes, row);
+        if (kind < 0) set_error(kDevBadIndex);
+        s_kind = kind;
+        s_row = row;
+        if (kind == 3 && c == 0 && p.inc_frame && frame >= 1 && frame - 1 < p.slots[p.slot].max_frames &&
+            (f == 0 ? p.mode0 : p.mode_next) == kEmbSynthCodes)
+          for (int k = 0; k < 37; ++k)
+            p.code_ring[((long long)p.slot * p.slots[p.slot].max_frames + frame - 1) * 37 + k] = codes[k];
+      }
+      named_bar_sync(1, kCW * 32);
+      kind = s_kind;
+      row = s_row;
+      for (int i = e0 + ctid; i < e1; i += kCW * 32) {
+        float v = 0.f;
+        if (kind == 0) v = __half2float(p.tok[(long long)row * D + i]);
+        else if (kind == 1) v = __half2float(p.audio[(long long)row * D + i]);
+        else if (kind == 2) v = p.rows_in[(long long)p.slot * D + i];
+        else if (kind == 4) v = p.voice[((long long)p.slot * p.max_voice + row) * D + i];
+        else if (kind == 3) {
+          // all 37 rows loaded first (one memory round trip), summed in the reference's order
+          __half r[37];
+          r[0] = p.audio[(long long)codes[0] * D + i];
+#pragma unroll
+          for (int k = 0; k < kNumAc; ++k) r[1 + k] = p.audio[(long long)(kAcBase + kAcStride * k + codes[1 + k]) * D + i];
+          float a = 0.f;
+#pragma unroll
+          for (int k = 0; k < 37; ++k) a += __half2float(r[k]);
+          v = a;
+        }
+        p.h[i] = v;
+      }
+      named_bar_sync(1, kCW * 32);
+      if (ctid == 0) red_release_add(p.bar, 1u);
+      ++phase;
+    }
+    for (int l = 0; l < L; ++l) {
+      const LayerPtrs& W = p.layers[l];
+      const int o0 = (int)(tiles_before % G);
+      const int o1 = (int)((tiles_before + kTilesQKV) % G);
+      const int o2 = (int)((tiles_before + kTilesQKV + kTilesO) % G);
+      const int o3 = (int)((tiles_before + kTilesQKV + kTilesO + kTilesW13) % G);
+      const int kl = 1 + 5 * l;
+      // ---- QKV (+ RoPE + KV append in the epilogue warp)
+      grid_wait(p, phase * G, ctid);
+      trace_mark(p, c, f, kl, 0, L, ctid);
+      const bool staged = prestage(p, &kvmap, s, l, pos, c, ctid, a_pending);
+      consume<6, 3, true>(p, s, it, rit, p.h, W.attn_norm, D, kTilesQKV, o0, c, G, cw, lane);
+      trace_mark(p, c, f, kl, 1, L, ctid);
+      ++phase;
+      // ---- attention
+      grid_wait(p, phase * G, ctid);
+      trace_mark(p, c, f, kl + 1, 0, L, ctid);
+      attention(p, &kvmap, s, ait, a_pending, staged, l, pos, c, G, cw, lane, ctid);
+      trace_mark(p, c, f, kl + 1, 1, L, ctid);
+      if (ctid == 0) red_release_add(p.bar, 1u);
+      ++phase;
+      // ---- o_proj + residual
+      grid_wait(p, phase * G, ctid);
+      trace_mark(p, c, f, kl + 2, 0, L, ctid);
+      consume<4, 4, false>(p, s, it, rit, p.att, nullptr, QD, kTilesO, o1, c, G, cw, lane);
+      trace_mark(p, c, f, kl + 2, 1, L, ctid);
+      ++phase;
+      // ---- gate/up + SwiGLU
+      grid_wait(p, phase * G, ctid);
+      trace_mark(p, c, f, kl + 3, 0, L, ctid);
+      consume<6, 3, true>(p, s, it, rit, p.h, W.ffn_norm, D, kTilesW13, o2, c, G, cw, lane);
+      trace_mark(p, c, f, kl + 3, 1, L, ctid);
+      ++phase;
+      // ---- down + residual
+      grid_wait(p, phase * G, ctid);
+      trace_mark(p, c, f, kl + 4, 0, L, ctid);
+      consume<2, 9, false>(p, s, it, rit, p.g, nullptr, F, kTilesW2, o3, c, G, cw, lane);
+      trace_mark(p, c, f, kl + 4, 1, L, ctid);
+      ++phase;
+      tiles_before += kTilesLayer;
+    }
+    // ---- FINAL norm (each CTA: full sum of squares, its slice of the output)
+    grid_wait(p, phase * G, ctid);
+    trace_mark(p, c, f, 1 + 5 * L, 0, L, ctid);
+    {
+      float ss = 0.f;
+      for (int i = ctid; i < D; i += kCW * 32) ss += p.h[i] * p.h[i];
+      ss = warp_sum(ss);
+      if (lane == 0) s.scratch[cw] = ss;
+      named_bar_sync(1, kCW * 32);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) tot += s.scratch[w];
+      const float rms = 1.0f / sqrtf(tot / (float)D + p.eps);
+      SlotState& st = p.slots[p.slot];
+      float* ring = (p.record && frame >= 0 && frame < st.max_frames)
+                        ? p.normed_ring + ((long long)p.slot * st.max_frames + frame) * D : nullptr;
+      for (int i = e0 + ctid; i < e1; i += kCW * 32) {
+        const float v = p.h[i] * rms * __half2float(p.final_norm[i]);
+        p.normed[i] = v;
+        if (ring) ring[i] = v;
+      }
+      named_bar_sync(1, kCW * 32);
+      if (ctid == 0) red_release_add(p.bar, 1u);
+      ++phase;
+    }
+  }
+  // an attention copy left in flight by an error must land before the CTA exits
+  if (ctid == 0 && a_pending) mbar_wait(s.afull, (ait - 1) & 1u, kDevTimeoutDrain);
+  // slot bookkeeping once every CTA has finished the last step
+  if (c == 0) {
+    grid_wait(p, phase * G, ctid);
+    if (ctid == 0 && !error_set()) {
+      SlotState& st = p.slots[p.slot];
+      st.pos = pos0 + p.n_frames;
+      if (p.inc_frame) st.frame = frame0 + p.n_frames;
+      const int lm = p.n_frames > 1 ? p.mode_next : p.mode0;
+      if (lm == kEmbSynthCodes)
+        for (int k = 0; k < 37; ++k) st.codes[k] = codes[k];
+    }
+  }
+}
+
+}  // namespace mk
+}  // namespace vx

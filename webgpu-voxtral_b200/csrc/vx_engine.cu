@@ -29,6 +29,7 @@
 #include "k_attn.cuh"
 #include "k_gemv.cuh"
 #include "k_misc.cuh"
+#include "k_step.cuh"
 
 using namespace vx;
 
@@ -144,6 +145,15 @@ struct vx_handle {
   // TP
   ncclComm_t comm = nullptr;
 
+  // persistent decode kernel (k_step.cuh): layer table and grid-barrier counter
+  bool use_mk = true;
+  mk::LayerPtrs* d_layers = nullptr;
+  unsigned* d_bar = nullptr;
+  unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
+  int prefetch_ahead = 8;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD)
+  int prestage_kv = 0;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV)
+  bool trace_armed = false;
+
   // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
   int parts = 7;          // kPartMisc | kPartGemv | kPartAttn
   bool profiling = false;
@@ -206,6 +216,48 @@ int prime_kernel_attrs(vx_handle* h) {
   CK(gemv_attr<6, 4, 3, kSwiglu, true>()); CK(gemv_attr<6, 4, 3, kResid, false>());
   CK(gemv_attr<2, 6, 3, kStore, true>());
   CK(cudaFuncSetAttribute(attn::k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  return VX_OK;
+}
+
+// n_frames consecutive backbone steps of one slot in ONE cooperative launch of the
+// persistent decode kernel (k_step.cuh).
+int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, int mode_next, bool inc_frame,
+                 bool record) {
+  if (n_frames <= 0) return VX_OK;
+  mk::StepParams sp{};
+  sp.layers = h->d_layers; sp.n_layers = h->L;
+  sp.tok = h->tok_emb; sp.vocab = h->V; sp.audio = h->audio_emb; sp.audio_rows = h->AV;
+  sp.rows_in = h->rows_in; sp.prompt = h->prompt; sp.voice = h->voice;
+  sp.max_seq = h->cfg.max_seq_len; sp.max_voice = h->cfg.max_voice_rows; sp.code_ring = h->code_ring;
+  const long long D = h->D;
+  sp.h = h->h + slot * D; sp.q = h->q + (long long)slot * h->QD; sp.att = h->att + (long long)slot * h->QD;
+  sp.g = h->g + (long long)slot * h->Fl; sp.normed = h->normed + slot * D; sp.normed_ring = h->normed_ring;
+  sp.final_norm = h->final_norm; sp.eps = h->cfg.norm_eps;
+  sp.kv = gemv::KvGeom{h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV, kPage};
+  sp.part = h->attn_part + (long long)slot * h->NKV * h->n_splits * attn::kGqa * attn::kPartStride;
+  sp.tickets = h->attn_tickets + (long long)slot * h->NKV;
+  sp.n_splits = h->n_splits; sp.rope_freq = h->rope_freq;
+  sp.slots = h->slots; sp.slot = slot; sp.bar = h->d_bar;
+  sp.trace = h->trace_armed ? h->d_trace : nullptr;
+  sp.prefetch_ahead = h->prefetch_ahead;
+  sp.prestage_kv = h->prestage_kv;
+  h->trace_armed = false;
+  sp.n_frames = n_frames; sp.mode0 = mode0; sp.token0 = token0; sp.mode_next = mode_next;
+  sp.inc_frame = inc_frame ? 1 : 0; sp.record = record ? 1 : 0;
+  CK(cudaMemsetAsync(h->d_bar, 0, sizeof(unsigned), h->stream));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(h->num_sms);
+  cfg.blockDim = dim3(mk::kThreads);
+  cfg.dynamicSmemBytes = mk::kSmemBytes;
+  cfg.stream = h->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  h->launches++;
+  CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps, h->kv_map, sp));
   return VX_OK;
 }
 
@@ -686,7 +738,8 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   h->max_pages = (c.max_seq_len + kPage - 1) / kPage;
   const long long total_pages = (long long)h->B * h->max_pages;
   h->kv_rows = total_pages * h->L * 2 * h->NKV * kPage;
-  h->n_splits = std::max(1, std::min(std::min(h->max_pages, attn::kMaxSplits), (2 * h->num_sms + h->NKV - 1) / h->NKV));
+  // one attention item per CTA: (kv heads x splits) <= SMs
+  h->n_splits = std::max(1, std::min(std::min(h->max_pages, attn::kMaxSplits), h->num_sms / h->NKV));
   size_t act = 0;
   auto f32n = [&](size_t n) { act += ((n * 4 + 255) & ~size_t(255)); };
   f32n(64);  // rope
@@ -775,6 +828,24 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   h->g_step.resize(h->B); h->g_fm.resize(h->B); h->g_frame_fm.resize(h->B); h->g_frame_bb.resize(h->B);
   if ((rc = make_kv_map(h))) { *out = h; return rc; }
   if ((rc = prime_kernel_attrs(h))) { *out = h; return rc; }
+  {
+    std::vector<mk::LayerPtrs> lp(h->L);
+    for (int l = 0; l < h->L; ++l)
+      lp[l] = mk::LayerPtrs{h->layers[l].wqkv, h->layers[l].wo, h->layers[l].w13, h->layers[l].w2,
+                            h->layers[l].attn_norm, h->layers[l].ffn_norm};
+    if (cudaMalloc((void**)&h->d_layers, sizeof(mk::LayerPtrs) * h->L + 256) != cudaSuccess ||
+        cudaMemcpy(h->d_layers, lp.data(), sizeof(mk::LayerPtrs) * h->L, cudaMemcpyHostToDevice) != cudaSuccess) {
+      *out = h; return h->fail(VX_E_NOMEM, "layer table");
+    }
+    h->d_bar = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(h->d_layers) + sizeof(mk::LayerPtrs) * h->L);
+    h->d_bar = reinterpret_cast<unsigned*>((reinterpret_cast<uintptr_t>(h->d_bar) + 127) & ~uintptr_t(127));
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->dev);
+    if (const char* pa = getenv("VX_PREFETCH_AHEAD")) h->prefetch_ahead = std::max(0, std::min(mk::kMaxPrefetchAhead, atoi(pa)));
+    if (const char* ps = getenv("VX_PRESTAGE_KV")) h->prestage_kv = atoi(ps) != 0;
+    const char* e = getenv("VX_NO_MEGAKERNEL");
+    h->use_mk = coop && h->tp == 1 && !(e && e[0] == '1');
+  }
   *out = h;
   return VX_OK;
 }
@@ -788,6 +859,8 @@ void vx_destroy(vx_handle* h) {
       if (g.exec) cudaGraphExecDestroy(g.exec);
   if (h->comm && g_nccl.commDestroy) g_nccl.commDestroy(h->comm);
   if (h->arena) cudaFree(h->arena);
+  if (h->d_layers) cudaFree(h->d_layers);
+  if (h->d_trace) cudaFree(h->d_trace);
   if (h->kv_pool) cudaFree(h->kv_pool);
   if (h->rope_freq) cudaFree(h->rope_freq);   // base of the activation block
   if (h->pinned) cudaFreeHost(h->pinned);
@@ -938,8 +1011,12 @@ int vx_prefill(vx_handle* h, int32_t slot, const int32_t* tokens, int32_t n, int
   u.set_mode = 1; u.mode = kEmbPrompt; u.token = 0;
   u.set_prompt_len = 1; u.prompt_len = p0 + n;
   if ((rc = slot_update(h, slot, u))) return rc;
-  for (int i = 0; i < n; ++i)
-    if ((rc = run_prog(h, kProgStep, slot))) return rc;
+  if (h->use_mk) {
+    if ((rc = launch_steps(h, slot, n, kEmbPrompt, 0, kEmbPrompt, false, false))) return rc;
+  } else {
+    for (int i = 0; i < n; ++i)
+      if ((rc = run_prog(h, kProgStep, slot))) return rc;
+  }
   h->pos_host[slot] += n;
   return finish(h);
 }
@@ -1067,11 +1144,24 @@ int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm) {
   const int steps = with_fm ? (f0 == 0 ? std::max(0, n_frames - 1) : n_frames) : n_frames;
   if ((rc = need_positions(h, slot, steps))) return rc;
   CK(cudaSetDevice(h->dev));
+  if (h->use_mk && !with_fm) {
+    // all frames in one launch: frame 0 is the AUDIO kick, later frames the synthetic codes
+    if (f0 == 0) rc = launch_steps(h, slot, n_frames, kEmbToken, kAudioKick, kEmbSynthCodes, true, true);
+    else rc = launch_steps(h, slot, n_frames, kEmbSynthCodes, 0, kEmbSynthCodes, true, true);
+    if (rc) return rc;
+    h->pos_host[slot] += n_frames;
+    h->frame_host[slot] = f0 + n_frames;
+    return VX_OK;
+  }
   for (int i = 0; i < n_frames; ++i) {
     const int f = f0 + i;
     if (with_fm) {
       if (f == 0) {
         if ((rc = run_prog(h, kProgFm, slot))) return rc;
+      } else if (h->use_mk) {
+        if ((rc = launch_steps(h, slot, 1, kEmbCodes, 0, kEmbCodes, false, true))) return rc;
+        if ((rc = run_prog(h, kProgFm, slot))) return rc;
+        h->pos_host[slot] += 1;
       } else {
         if (i == 0 || f0 + i == 1) {
           if ((rc = set_slot_fields(h, slot, kEmbCodes, 0))) return rc;
@@ -1200,6 +1290,24 @@ int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, dou
   CK(cudaMemcpyAsync(&h->slots[slot], &saved, sizeof(SlotState), cudaMemcpyHostToDevice, h->stream));
   if (rc) return rc;
   if (out_bytes) out_bytes[0] = gemv_bytes;
+  return finish(h);
+}
+
+int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n, int32_t* dims) {
+  if (!h) return VX_E_INVALID;
+  CK(cudaSetDevice(h->dev));
+  const size_t per = (size_t)mk::kTraceFrames * (2 + 5 * h->L) * 3;
+  const size_t total = per * h->num_sms;
+  if (dims) { dims[0] = h->num_sms; dims[1] = mk::kTraceFrames; dims[2] = 2 + 5 * h->L; dims[3] = 3; }
+  if (mode == 2) return VX_OK;   // dimensions only
+  if (mode == 1) {
+    if (!h->d_trace && cudaMalloc((void**)&h->d_trace, total * 8) != cudaSuccess) return h->fail(VX_E_NOMEM, "trace");
+    CK(cudaMemsetAsync(h->d_trace, 0, total * 8, h->stream));
+    h->trace_armed = true;
+    return VX_OK;
+  }
+  if (!out || !h->d_trace) return h->fail(VX_E_STATE, "no trace recorded");
+  CK(cudaMemcpyAsync(out, h->d_trace, std::min(n, total) * 8, cudaMemcpyDeviceToHost, h->stream));
   return finish(h);
 }
 

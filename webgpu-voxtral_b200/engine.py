@@ -101,6 +101,7 @@ def load_library():
         "vx_launch_count": (ctypes.c_int64, [H]),
         "vx_profile_step": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p,
                                            ctypes.POINTER(ctypes.c_double)]),
+        "vx_trace": (ctypes.c_int, [H, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, _i32p]),
         "vx_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p, _u8p]),
         "vx_tp_init": (ctypes.c_int, [H, ctypes.c_char_p, _u8p]),
     }
@@ -264,6 +265,20 @@ class VoxtralEngine:
         self._check(load_library().vx_profile_step(self._h, slot, reps, _p(ms, _f32p), ctypes.byref(by)))
         return {"step_ms": float(ms[0]), "gemv_ms": float(ms[1]), "attn_ms": float(ms[2]),
                 "gemv_bytes": float(by.value)}
+
+    def trace_arm(self):
+        """Record phase timestamps of the next persistent-kernel launch (first 2 steps)."""
+        self._check(load_library().vx_trace(self._h, 1, None, 0, None))
+
+    def trace_read(self) -> np.ndarray:
+        """[cta, step, phase, {released, consumers done, epilogue arrival}] in ns (0 = not recorded)."""
+        L = load_library()
+        dims = np.zeros(4, np.int32)
+        self._check(L.vx_trace(self._h, 2, None, 0, _p(dims, _i32p)))
+        n = int(np.prod(dims))
+        out = np.zeros(n, np.uint64)
+        self._check(L.vx_trace(self._h, 0, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), n, _p(dims, _i32p)))
+        return out.reshape(tuple(int(d) for d in dims))
 
     # ------------------------------------------------------------------ steps
     def prefill(self, tokens, audioTokenStart: int = 0, audioTokenCount: int = 0, voiceEmbeddings=None, slot: int = 0):
