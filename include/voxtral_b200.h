@@ -193,6 +193,24 @@ int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t*
 int vx_nccl_unique_id(const char* nccl_lib, uint8_t out[128]);
 int vx_tp_init(vx_handle* h, const char* nccl_lib, const uint8_t id[128]);
 
+/* LM-head argmax for callers that cannot allocate device memory.  No counterpart in
+ * the reference.  Callers that cannot call cudaMalloc (a real-time audio callback, where
+ * cudaMalloc may synchronise the device and block; a host framework that owns all
+ * device memory through its own arena) cannot create a vx_handle, but can pass their
+ * own device buffers here.  Computes *out_index = argmax_r (W[r,:] . x) (maximum value,
+ * lowest index on ties) and *out_value = that maximum (nullable), the same greedy
+ * choice as vx_backbone_step's argmax_out, in one kernel that allocates nothing.
+ * weight: device f16 bits [rows][dim], 16-byte aligned; x: device f32 [dim];
+ * out_index / out_value: device; stream: cudaStream_t (NULL = default stream);
+ * err (nullable): receives a message.  Limits: rows <= 2,097,152, dim a multiple of 8
+ * and <= 16,384 (VX_E_RANGE beyond them).  Its scratch is a 65,792-byte static device
+ * array that every GPU loading the library holds until the process exits; the first
+ * call on a device looks up that array's address (call it once before any stream
+ * capture).  All calls on a device share the array, so calls that overlap on the GPU
+ * race; calls ordered on one stream do not. */
+int vx_lm_head_argmax_noalloc(const uint16_t* weight, const float* x, int32_t rows, int32_t dim, int32_t* out_index,
+                              float* out_value, void* stream, char* err, size_t err_len);
+
 #ifdef __cplusplus
 }
 #endif

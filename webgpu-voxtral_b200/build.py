@@ -16,8 +16,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libvoxtral_b200.so")
-SOURCES = ["vx_engine.cu"]
-DEPS = ["vx_engine.cu", "k_gemv.cuh", "k_attn.cuh", "k_misc.cuh", "vx_common.cuh", "vx_rng.h"]
+SOURCES = ["vx_engine.cu", "vx_noalloc.cu"]
+DEPS = ["vx_engine.cu", "vx_noalloc.cu", "k_gemv.cuh", "k_attn.cuh", "k_misc.cuh", "k_step.cuh", "vx_common.cuh", "vx_rng.h"]
 
 
 def nvcc() -> str:
