@@ -181,9 +181,9 @@ int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, dou
 /* Phase tracing of the persistent decode kernel (the reference records stage
  * wall-clock times only, src/engine.ts:2428-2601).  mode 1 arms tracing for the next
  * persistent launch on this handle; mode 0 copies the trace out: %globaltimer stamps
- * (ns) indexed [cta][step < 2][phase][3] = {consumers released by the grid barrier,
- * consumers done, epilogue arrival}; mode 2 only reports the dimensions.  dims
- * (nullable) receives {ctas, steps, phases, 3}. */
+ * (ns) indexed [cta][step < 2][phase][4] = {consumers released by the grid barrier,
+ * consumers done, epilogue arrival, consumers' prologue done}; mode 2 only reports the
+ * dimensions.  dims (nullable) receives {ctas, steps, phases, 4}. */
 int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t* dims);
 
 /* Tensor parallelism over NCCL (batch-1 latency, heads and FFN columns

@@ -26,7 +26,7 @@ constexpr int kGqa = 4;              // query heads per KV head
 constexpr int kHd = 128;
 constexpr int kPage = 64;
 constexpr int kStageBytes = 4 * 8192;  // K box0, K box1, V box0, V box1 (64 rows x 64 cols f16 each)
-constexpr int kPartStride = 2 + kHd;   // (m, l, o[128]) per head
+constexpr int kPartStride = 4 + kHd;   // (m, l, -, -, o[128]) per head: o 16-byte aligned
 constexpr int kMaxSplits = 64;         // splits per (row, kv head); the combine holds one weight per split
 constexpr size_t kSmemBytes = 2 * (size_t)kStageBytes + 1024 /*align slack*/ + 64;
 

@@ -52,6 +52,8 @@ constexpr size_t kSmemBytes = (size_t)kOffScratch + kScratchBytes + 1024;   // +
 // tiles per GEMV phase (rows per tile: QKV 6, O 4, W13 3 outputs, W2 2)
 constexpr int kTilesQKV = QKVD / 6, kTilesO = D / 4, kTilesW13 = F / 3, kTilesW2 = D / 2;
 constexpr int kTilesLayer = kTilesQKV + kTilesO + kTilesW13 + kTilesW2;
+// tiles per reduction group (group outputs TG * rows-per-tile <= 32)
+constexpr int kTgQKV = 1, kTgO = 1, kTgW13 = 1, kTgW2 = 1;
 
 struct LayerPtrs {
   const __half *wqkv, *wo, *w13, *w2, *attn_norm, *ffn_norm;
@@ -153,11 +155,12 @@ __device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, 
   if (lane == 0) red_release_add(p.bar, 1u);
 }
 // Phase trace (globaltimer ns) for the first kTraceFrames steps when p.trace is set:
-// [cta][phase][0] = consumers released, [1] = consumers done, [2] = epilogue arrival.
+// [cta][phase][0] = consumers released, [1] = consumers done, [2] = epilogue arrival,
+// [3] = consumers' x' prologue done (GEMV phases).
 constexpr int kTraceFrames = 2;
 __device__ __forceinline__ void trace_mark(const StepParams& p, int c, int f, int kl, int which, int L, int t0) {
   if (p.trace && f < kTraceFrames && t0 == 0)
-    p.trace[(((long long)c * kTraceFrames + f) * (2 + 5 * L) + kl) * 3 + which] = globaltimer();
+    p.trace[(((long long)c * kTraceFrames + f) * (2 + 5 * L) + kl) * 4 + which] = globaltimer();
 }
 
 __device__ __forceinline__ int first_tile(int c, int off, int G) { return (c - off % G + G) % G; }
@@ -206,10 +209,15 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 }
 
 // ---------------------------------------------------------------- consumer GEMV phase
-template <int R, int CPL, bool NORM>
+// Tiles are consumed in groups of TG: each ring stage is released right after its
+// FMAs, but the cross-lane reduction, the reduction-slot handoff and the epilogue run
+// once per group (TG*R <= 32 outputs), which amortises their latency over TG tiles.
+template <int R, int CPL, bool NORM, int TG>
 __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& it, uint32_t& rit, const float* x,
-                                       const __half* norm_w, int kc, int T, int off, int c, int G, int cw, int lane) {
-  constexpr int P = gemv::Pow2<R>::v;
+                                       const __half* norm_w, int kc, int T, int off, int c, int G, int cw, int lane,
+                                       int pos, int f, int kl) {
+  static_assert(R * TG <= kMaxVals, "group too large");
+  constexpr int P = gemv::Pow2<R * TG>::v;
   // x' slice in registers.  For the RMSNorm variants each warp's slice (CPL x 128
   // columns; the 8 slices partition the row) also gives its partial sum of squares,
   // so the norm costs one load round and one named barrier.
@@ -242,35 +250,43 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
       xr[j][2] = xr[j][2] * rms * wn[j][1].x; xr[j][3] = xr[j][3] * rms * wn[j][1].y;
     }
   }
+  trace_mark(p, c, f, kl, 3, p.n_layers, cw * 32 + lane);
   const int my_idx = gemv::transpose_index<P>(lane);
-  const bool writer = lane < P && my_idx < R;
+  const bool writer = lane < P && my_idx < R * TG;
   const uint32_t rowbytes = (uint32_t)kc * 2u;
-  for (int t = first_tile(c, off, G); t < T; t += G, ++it, ++rit) {
-    const int st = it % kStages;
-    if (!mbar_wait(&s.full[st], (it / kStages) & 1u, kDevTimeoutFull)) return false;
-    float acc[R];
+  for (int g0 = first_tile(c, off, G); g0 < T; g0 += TG * G, ++rit) {
+    float acc[TG][R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
-    const uint8_t* base = s.ring + (size_t)st * kStageBytes + (size_t)(cw * 128 + lane * 4) * 2;
+    for (int u = 0; u < TG; ++u)
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+      for (int r = 0; r < R; ++r) acc[u][r] = 0.f;
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        const uint2 wv = *reinterpret_cast<const uint2*>(base + (size_t)r * rowbytes + (size_t)j * kCW * 256);
-        const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-        const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
-        float a = acc[r];
-        a = fmaf(w01.x, xr[j][0], a);
-        a = fmaf(w01.y, xr[j][1], a);
-        a = fmaf(w23.x, xr[j][2], a);
-        a = fmaf(w23.y, xr[j][3], a);
-        acc[r] = a;
-      }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&s.empty[st]);
+    for (int u = 0; u < TG; ++u) {
+      if (g0 + u * G >= T) break;
+      const int st = it % kStages;
+      if (!mbar_wait(&s.full[st], (it / kStages) & 1u, kDevTimeoutFull)) return false;
+      const uint8_t* base = s.ring + (size_t)st * kStageBytes + (size_t)(cw * 128 + lane * 4) * 2;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+          const uint2 wv = *reinterpret_cast<const uint2*>(base + (size_t)r * rowbytes + (size_t)j * kCW * 256);
+          const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+          const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+          float a = acc[u][r];
+          a = fmaf(w01.x, xr[j][0], a);
+          a = fmaf(w01.y, xr[j][1], a);
+          a = fmaf(w23.x, xr[j][2], a);
+          a = fmaf(w23.y, xr[j][3], a);
+          acc[u][r] = a;
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[st]);
+      ++it;
+    }
     float v[P];
 #pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = i < R ? acc[i] : 0.f;
+    for (int i = 0; i < P; ++i) v[i] = i < R * TG ? acc[i / R][i % R] : 0.f;
     const float rv = gemv::transpose_reduce<P>(v, lane);
     const int rs = rit % kRedSlots;
     if (!mbar_wait(&s.rempty[rs], ((rit / kRedSlots) & 1u) ^ 1u, kDevTimeoutRed)) return false;
@@ -283,37 +299,40 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
 
 // ---------------------------------------------------------------- epilogue GEMV phase
 // EPI: gemv::kQkv (rows -> q / K / V with RoPE), kResid (y += ), kSwiglu (g = silu(a)*b)
-template <int R, int EPI>
+template <int R, int EPI, int TG>
 __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t& rit, float* y, int rows, int T,
                                          int off, int c, int G, int lane, int layer, int pos) {
   constexpr int ORT = EPI == gemv::kSwiglu ? R / 2 : R;
-  for (int t = first_tile(c, off, G); t < T; t += G, ++rit) {
+  for (int g0 = first_tile(c, off, G); g0 < T; g0 += TG * G, ++rit) {
     const int rs = rit % kRedSlots;
+    // lane -> (tile u of the group, row r of the tile)
+    const int u = lane / R, r = lane % R;
+    const int t = g0 + u * G;
+    const bool live = lane < R * TG && t < T;
     float yold = 0.f;   // residual row loaded before the wait so its latency overlaps it
     if constexpr (EPI == gemv::kResid) {
-      const int row = t * ORT + lane;
-      if (lane < R && row < rows) yold = y[row];
+      const int row = t * ORT + r;
+      if (live && row < rows) yold = y[row];
     }
     if (!mbar_wait(&s.rfull[rs], (rit / kRedSlots) & 1u, kDevTimeoutRed)) return false;
     float val = 0.f;
-    if (lane < R) {
+    if (lane < R * TG) {
 #pragma unroll
       for (int w = 0; w < kCW; ++w) val += s.red[(rs * kCW + w) * kMaxVals + lane];
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.rempty[rs]);
-    const int r = lane;
     if constexpr (EPI == gemv::kResid) {
       const int row = t * ORT + r;
-      if (r < R && row < rows) y[row] = yold + val;
+      if (live && row < rows) y[row] = yold + val;
     } else if constexpr (EPI == gemv::kSwiglu) {
       const float up = __shfl_down_sync(0xffffffffu, val, ORT);
       const int row = t * ORT + r;
-      if (r < ORT && row < rows) y[row] = swiglu(val, up);
+      if (live && r < ORT && row < rows) y[row] = swiglu(val, up);
     } else {
       const float other = __shfl_xor_sync(0xffffffffu, val, 1);
       const int row = t * R + r;
-      if (r < R && row < rows) {
+      if (live && row < rows) {
         float out = val;
         if (row < QD + KVD) {
           const float ang = (float)pos * p.rope_freq[(row & 127) >> 1];
@@ -348,6 +367,18 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
 // ---------------------------------------------------------------- attention phase
 // Split-KV flash decode over the pages of (kv head, split) items dealt to this CTA.
 // 8 warps: warps 0-3 take page 2i of a pair, warps 4-7 page 2i+1, 16 positions each.
+// Split plan of a step: splits of >= 2 pages (one TMA pair), at most p.n_splits per KV
+// head; n_used splits hold positions.  Partials live at
+// part[((kvh * p.n_splits + split) * GQA + head) * kPartStride] = {max, sum, -, -, o[128]}.
+constexpr int PS = attn::kPartStride;
+constexpr int kMaxUsed = 9;   // splits per KV head: the last split merges them in one load round
+__device__ __forceinline__ void split_plan(const StepParams& p, int pos, int& npages, int& pps, int& n_used) {
+  npages = (pos + 1 + 63) / 64;
+  const int cap = min(p.n_splits, kMaxUsed);
+  pps = max(2, (npages + cap - 1) / cap);
+  n_used = (npages + pps - 1) / pps;
+}
+
 // TMA of K/V pages [pp, pp+npair) of one KV head into the attention buffer (thread 0).
 __device__ __forceinline__ void issue_pair(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int kvh,
                                            int pp, int npair) {
@@ -370,11 +401,11 @@ __device__ __forceinline__ void issue_pair(const StepParams& p, const CUtensorMa
 __device__ __forceinline__ bool prestage(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int pos,
                                          int c, int ctid, bool& a_pending) {
   if (!p.prestage_kv || c >= NKV * p.n_splits) return false;
-  const int npages = (pos + 1 + 63) / 64;
-  const int pps = (npages + p.n_splits - 1) / p.n_splits;
+  int npages, pps, n_used;
+  split_plan(p, pos, npages, pps, n_used);
   const int kvh = c / p.n_splits, split = c % p.n_splits;
+  if (split >= n_used) return false;
   const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
-  if (pg0 >= pg1) return false;
   if (ctid == 0 && !error_set()) {
     a_pending = true;
     issue_pair(p, kvmap, s, layer, kvh, pg0, min(2, pg1 - pg0));
@@ -388,16 +419,16 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
                                           bool& a_pending, bool staged, int layer, int pos, int c, int G, int cw,
                                           int lane, int ctid) {
   const int seq = pos + 1;
-  const int npages = (seq + 63) / 64;
-  const int pps = (npages + p.n_splits - 1) / p.n_splits;
+  int npages, pps, n_used;
+  split_plan(p, pos, npages, pps, n_used);
   const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
   const float scale = 0.08838834764831845f;   // 1/sqrt(128) rounded to f32
   const int g = lane >> 2, hq = g & 3;
   const bool lo_part = g >= 4;
   const int half_pair = cw >> 2, grp = cw & 3;
-  __shared__ int s_last;
   for (int item = c; item < NKV * p.n_splits; item += G) {
     const int kvh = item / p.n_splits, split = item % p.n_splits;
+    if (split >= n_used) continue;   // uniform: no positions in this split
     const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
     float m_run = -INFINITY, l_run = 0.f;
     float o[16][4];
@@ -520,7 +551,7 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
       }
     }
     named_bar_sync(1, kCW * 32);
-    float* part = p.part + ((long long)kvh * p.n_splits + split) * (GQA * attn::kPartStride);
+    float* part = p.part + ((long long)kvh * p.n_splits + split) * (GQA * PS);
     for (int idx = ctid; idx < GQA * HD; idx += kCW * 32) {
       const int h = idx / HD, d = idx % HD;
       float M = -INFINITY;
@@ -536,43 +567,44 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
           O += ww[2 + d] * f;
         }
       }
-      part[h * attn::kPartStride + 2 + d] = O;
-      if (d == 0) { part[h * attn::kPartStride] = M; part[h * attn::kPartStride + 1] = L; }
+      part[h * PS + 4 + d] = O;
+      if (d == 0) { part[h * PS] = M; part[h * PS + 1] = L; }
     }
     named_bar_sync(1, kCW * 32);
-    if (ctid == 0) s_last = (atom_add_acq_rel(&p.tickets[kvh], 1) == p.n_splits - 1);
+    // The last split of this KV head to finish merges all n_used splits into att.
+    // Each thread owns 2 output dims of one head and issues all its loads at once.
+    int* s_flag = reinterpret_cast<int*>(s.scratch + 1020);
+    if (ctid == 0) *s_flag = (atom_add_acq_rel(&p.tickets[kvh], 1) == n_used - 1);
     named_bar_sync(1, kCW * 32);
-    if (s_last) {
-      const float* pb = p.part + (long long)kvh * p.n_splits * (GQA * attn::kPartStride);
-      const int n_used = min(p.n_splits, (npages + pps - 1) / pps);
-      float* sw = s.scratch;                            // [64 splits][4 heads]
-      if (cw < GQA) {
-        const int h = cw;
-        float ms[2], ls[2], M = -INFINITY;
+    if (*s_flag) {
+      const int h = ctid >> 6, d0 = (ctid & 63) * 2;
+      const float* base = p.part + ((long long)kvh * p.n_splits * GQA + h) * PS;
+      float mm[kMaxUsed], ll[kMaxUsed];
+      float2 oo[kMaxUsed];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int sp = lane + 32 * j;
-          ms[j] = sp < n_used ? __ldcg(pb + sp * GQA * attn::kPartStride + h * attn::kPartStride) : -INFINITY;
-          ls[j] = sp < n_used ? __ldcg(pb + sp * GQA * attn::kPartStride + h * attn::kPartStride + 1) : 0.f;
-          M = fmaxf(M, ms[j]);
+      for (int sp = 0; sp < kMaxUsed; ++sp) {
+        if (sp < n_used) {
+          const float* b = base + (long long)sp * GQA * PS;
+          mm[sp] = __ldcg(b);
+          ll[sp] = __ldcg(b + 1);
+          oo[sp] = __ldcg(reinterpret_cast<const float2*>(b + 4 + d0));
+        } else {
+          mm[sp] = -INFINITY; ll[sp] = 0.f; oo[sp] = make_float2(0.f, 0.f);
         }
-        M = warp_max(M);
-        float f[2], L = 0.f;
-#pragma unroll
-        for (int j = 0; j < 2; ++j) { f[j] = ms[j] == -INFINITY ? 0.f : expf(ms[j] - M); L += ls[j] * f[j]; }
-        L = warp_sum(L);
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          if (lane + 32 * j < n_used) sw[(lane + 32 * j) * GQA + h] = f[j] / L;
       }
-      named_bar_sync(1, kCW * 32);
-      for (int idx = ctid; idx < GQA * HD; idx += kCW * 32) {
-        const int h = idx / HD, d = idx % HD;
-        float O = 0.f;
-#pragma unroll 8
-        for (int sp = 0; sp < n_used; ++sp) O += __ldcg(pb + sp * GQA * attn::kPartStride + h * attn::kPartStride + 2 + d) * sw[sp * GQA + h];
-        p.att[(kvh * GQA + h) * HD + d] = O;
+      float M = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < kMaxUsed; ++sp) M = fmaxf(M, mm[sp]);
+      float L = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxUsed; ++sp) {
+        const float w = mm[sp] == -INFINITY ? 0.f : expf(mm[sp] - M);
+        L += ll[sp] * w;
+        a0 += w * oo[sp].x;
+        a1 += w * oo[sp].y;
       }
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      *reinterpret_cast<float2*>(p.att + (kvh * GQA + h) * HD + d0) = make_float2(a0 * inv, a1 * inv);
       if (ctid == 0) p.tickets[kvh] = 0;
     }
     named_bar_sync(1, kCW * 32);
@@ -682,13 +714,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         const int o2 = (int)((tiles_before + kTilesQKV + kTilesO) % G);
         const int o3 = (int)((tiles_before + kTilesQKV + kTilesO + kTilesW13) % G);
         const int kl = 1 + 5 * l;
-        if (!epilogue<6, gemv::kQkv>(p, s, rit, nullptr, QKVD, kTilesQKV, o0, c, G, lane, l, pos)) return;
+        if (!epilogue<6, gemv::kQkv, kTgQKV>(p, s, rit, nullptr, QKVD, kTilesQKV, o0, c, G, lane, l, pos)) return;
         trace_mark(p, c, f, kl, 2, L, lane);
-        if (!epilogue<4, gemv::kResid>(p, s, rit, p.h, D, kTilesO, o1, c, G, lane, l, pos)) return;
+        if (!epilogue<4, gemv::kResid, kTgO>(p, s, rit, p.h, D, kTilesO, o1, c, G, lane, l, pos)) return;
         trace_mark(p, c, f, kl + 2, 2, L, lane);
-        if (!epilogue<6, gemv::kSwiglu>(p, s, rit, p.g, F, kTilesW13, o2, c, G, lane, l, pos)) return;
+        if (!epilogue<6, gemv::kSwiglu, kTgW13>(p, s, rit, p.g, F, kTilesW13, o2, c, G, lane, l, pos)) return;
         trace_mark(p, c, f, kl + 3, 2, L, lane);
-        if (!epilogue<2, gemv::kResid>(p, s, rit, p.h, D, kTilesW2, o3, c, G, lane, l, pos)) return;
+        if (!epilogue<2, gemv::kResid, kTgW2>(p, s, rit, p.h, D, kTilesW2, o3, c, G, lane, l, pos)) return;
         trace_mark(p, c, f, kl + 4, 2, L, lane);
         tiles_before += kTilesLayer;
       }
@@ -760,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       grid_wait(p, phase * G, ctid);
       trace_mark(p, c, f, kl, 0, L, ctid);
       const bool staged = prestage(p, &kvmap, s, l, pos, c, ctid, a_pending);
-      consume<6, 3, true>(p, s, it, rit, p.h, W.attn_norm, D, kTilesQKV, o0, c, G, cw, lane);
+      consume<6, 3, true, kTgQKV>(p, s, it, rit, p.h, W.attn_norm, D, kTilesQKV, o0, c, G, cw, lane, pos, f, kl);
       trace_mark(p, c, f, kl, 1, L, ctid);
       ++phase;
       // ---- attention
@@ -773,19 +805,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       // ---- o_proj + residual
       grid_wait(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 2, 0, L, ctid);
-      consume<4, 4, false>(p, s, it, rit, p.att, nullptr, QD, kTilesO, o1, c, G, cw, lane);
+      consume<4, 4, false, kTgO>(p, s, it, rit, p.att, nullptr, QD, kTilesO, o1, c, G, cw, lane, pos, f, kl + 2);
       trace_mark(p, c, f, kl + 2, 1, L, ctid);
       ++phase;
       // ---- gate/up + SwiGLU
       grid_wait(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 3, 0, L, ctid);
-      consume<6, 3, true>(p, s, it, rit, p.h, W.ffn_norm, D, kTilesW13, o2, c, G, cw, lane);
+      consume<6, 3, true, kTgW13>(p, s, it, rit, p.h, W.ffn_norm, D, kTilesW13, o2, c, G, cw, lane, pos, f, kl + 3);
       trace_mark(p, c, f, kl + 3, 1, L, ctid);
       ++phase;
       // ---- down + residual
       grid_wait(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 4, 0, L, ctid);
-      consume<2, 9, false>(p, s, it, rit, p.g, nullptr, F, kTilesW2, o3, c, G, cw, lane);
+      consume<2, 9, false, kTgW2>(p, s, it, rit, p.g, nullptr, F, kTilesW2, o3, c, G, cw, lane, pos, f, kl + 4);
       trace_mark(p, c, f, kl + 4, 1, L, ctid);
       ++phase;
       tiles_before += kTilesLayer;

@@ -151,7 +151,7 @@ struct vx_handle {
   unsigned* d_bar = nullptr;
   unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
   int prefetch_ahead = 8;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD)
-  int prestage_kv = 0;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV)
+  int prestage_kv = 1;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV)
   bool trace_armed = false;
 
   // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
@@ -1296,9 +1296,9 @@ int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, dou
 int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n, int32_t* dims) {
   if (!h) return VX_E_INVALID;
   CK(cudaSetDevice(h->dev));
-  const size_t per = (size_t)mk::kTraceFrames * (2 + 5 * h->L) * 3;
+  const size_t per = (size_t)mk::kTraceFrames * (2 + 5 * h->L) * 4;
   const size_t total = per * h->num_sms;
-  if (dims) { dims[0] = h->num_sms; dims[1] = mk::kTraceFrames; dims[2] = 2 + 5 * h->L; dims[3] = 3; }
+  if (dims) { dims[0] = h->num_sms; dims[1] = mk::kTraceFrames; dims[2] = 2 + 5 * h->L; dims[3] = 4; }
   if (mode == 2) return VX_OK;   // dimensions only
   if (mode == 1) {
     if (!h->d_trace && cudaMalloc((void**)&h->d_trace, total * 8) != cudaSuccess) return h->fail(VX_E_NOMEM, "trace");
