@@ -172,36 +172,42 @@ __device__ __constant__ int kTilesOf[4] = {kTilesQKV, kTilesO, kTilesW13, kTiles
 __device__ __constant__ int kTilePrefix[4] = {0, kTilesQKV, kTilesQKV + kTilesO, kTilesQKV + kTilesO + kTilesW13};
 struct Cursor {
   int f, l, k, t;
-  long long tb;   // tiles of all earlier layers (sets the dealing offset)
+  int off;                    // dealing offset of the current phase: (tiles of earlier phases) mod G
+  const __half *w0, *w1, *w2, *w3;   // weights of layer l (cached: no global load per tile)
 };
-__device__ __forceinline__ void cursor_fix(Cursor& x, int c, int G, int L) {
+__device__ __forceinline__ void cursor_layer(const StepParams& p, Cursor& x) {
+  const LayerPtrs& W = p.layers[x.l];
+  x.w0 = W.wqkv; x.w1 = W.wo; x.w2 = W.w13; x.w3 = W.w2;
+}
+__device__ __forceinline__ void cursor_fix(const StepParams& p, Cursor& x, int c, int G, int L) {
   while (x.t >= kTilesOf[x.k]) {
+    x.off = (x.off + kTilesOf[x.k]) % G;
     if (++x.k == 4) {
       x.k = 0;
-      x.tb += kTilesLayer;
       if (++x.l == L) { x.l = 0; ++x.f; }
+      if (x.f < p.n_frames) cursor_layer(p, x);
     }
-    x.t = first_tile(c, (int)((x.tb + kTilePrefix[x.k]) % G), G);
+    x.t = first_tile(c, x.off, G);
   }
 }
-__device__ __forceinline__ void cursor_start(Cursor& x, int c, int G, int L) {
-  x.f = 0; x.l = 0; x.k = 0; x.tb = 0; x.t = first_tile(c, 0, G);
-  cursor_fix(x, c, G, L);
+__device__ __forceinline__ void cursor_start(const StepParams& p, Cursor& x, int c, int G, int L) {
+  x.f = 0; x.l = 0; x.k = 0; x.off = 0; x.t = first_tile(c, 0, G);
+  cursor_layer(p, x);
+  cursor_fix(p, x, c, G, L);
 }
-__device__ __forceinline__ void cursor_next(Cursor& x, int c, int G, int L) {
+__device__ __forceinline__ void cursor_next(const StepParams& p, Cursor& x, int c, int G, int L) {
   x.t += G;
-  cursor_fix(x, c, G, L);
+  cursor_fix(p, x, c, G, L);
 }
 // Source of a tile: first chunk (and the SwiGLU "up" chunk), bytes per chunk.
 __device__ __forceinline__ void tile_src(const StepParams& p, const Cursor& x, const __half*& a, const __half*& b,
                                          uint32_t& bytes, int& ort) {
-  const LayerPtrs& W = p.layers[x.l];
   b = nullptr;
   switch (x.k) {
-    case 0: ort = 6; a = W.wqkv + (long long)x.t * 6 * D; bytes = min(6, QKVD - x.t * 6) * D * 2; break;
-    case 1: ort = 4; a = W.wo + (long long)x.t * 4 * QD; bytes = min(4, D - x.t * 4) * QD * 2; break;
-    case 2: ort = 3; a = W.w13 + (long long)x.t * 3 * D; b = a + (long long)F * D; bytes = min(3, F - x.t * 3) * D * 2; break;
-    default: ort = 2; a = W.w2 + (long long)x.t * 2 * F; bytes = min(2, D - x.t * 2) * F * 2; break;
+    case 0: ort = 6; a = x.w0 + (long long)x.t * 6 * D; bytes = min(6, QKVD - x.t * 6) * D * 2; break;
+    case 1: ort = 4; a = x.w1 + (long long)x.t * 4 * QD; bytes = min(4, D - x.t * 4) * QD * 2; break;
+    case 2: ort = 3; a = x.w2 + (long long)x.t * 3 * D; b = a + (long long)F * D; bytes = min(3, F - x.t * 3) * D * 2; break;
+    default: ort = 2; a = x.w3 + (long long)x.t * 2 * F; bytes = min(2, D - x.t * 2) * F * 2; break;
   }
 }
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
@@ -667,14 +673,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       const uint64_t pol = policy_evict_first();
       uint32_t it = 0;
       Cursor cur, ahead;
-      cursor_start(cur, c, G, L);
-      cursor_start(ahead, c, G, L);
+      cursor_start(p, cur, c, G, L);
+      cursor_start(p, ahead, c, G, L);
       for (int i = 0; i < p.prefetch_ahead && ahead.f < p.n_frames; ++i) {
         const __half *a, *b; uint32_t bytes; int ort;
         tile_src(p, ahead, a, b, bytes, ort);
         prefetch_l2(a, bytes);
         if (b) prefetch_l2(b, bytes);
-        cursor_next(ahead, c, G, L);
+        cursor_next(p, ahead, c, G, L);
       }
       while (cur.f < p.n_frames) {
         const int st = it % kStages;
@@ -686,12 +692,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         bulk_g2s(dst, a, bytes, &s.full[st], pol);
         if (b) bulk_g2s(dst + (size_t)ort * D * 2, b, bytes, &s.full[st], pol);   // SwiGLU up rows after the gate rows
         ++it;
-        cursor_next(cur, c, G, L);
+        cursor_next(p, cur, c, G, L);
         if (p.prefetch_ahead > 0 && ahead.f < p.n_frames) {
           tile_src(p, ahead, a, b, bytes, ort);
           prefetch_l2(a, bytes);
           if (b) prefetch_l2(b, bytes);
-          cursor_next(ahead, c, G, L);
+          cursor_next(p, ahead, c, G, L);
         }
       }
       // drain the copies still in flight
