@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--voice", type=int, default=N_VOICE, help="voice rows in the prompt (C2: 100)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="dp", choices=["dp", "tp"],
+                    help="N > 1: dp = one utterance per GPU (weak scaling); tp = one utterance over N GPUs")
+    ap.add_argument("--c3-frames", type=int, default=40, help="frames of the backbone+FM (C3) sample; 0 = skip")
     return ap.parse_args()
 
 
@@ -67,11 +70,11 @@ def measured_peaks():
 
 
 def ncu_traffic():
-    """Per-launch DRAM bytes of the weight-streaming GEMV from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "k_gemv_c2.md")
+    """DRAM bytes per decoded frame per layer of the persistent kernel (committed ncu summary)."""
+    p = os.path.join(ROOT, "profiles", "k_decode_steps_c2.md")
     if not os.path.exists(p):
         return None
-    m = re.search(r"dram_bytes_per_step:\s*([0-9.eE+]+)", open(p).read())
+    m = re.search(r"dram_bytes_per_frame_per_layer:\s*([0-9.eE+]+)", open(p).read())
     return float(m.group(1)) if m else None
 
 
@@ -116,6 +119,15 @@ class Clocks:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def nccl_lib_path():
+    try:
+        import nvidia.nccl
+        p = os.path.join(list(nvidia.nccl.__path__)[0], "lib", "libnccl.so.2")
+        return p if os.path.exists(p) else None
+    except Exception:  # noqa: BLE001
+        return None
 
 
 def cpu_sample(n_layers: int, seconds: float, n_frames_min: int = 2):
@@ -185,16 +197,22 @@ def run_b200(args):
     torch.cuda.set_device(local)
     vdist.init(timeout_s=300)
     F = args.frames
+    tp = world if (args.mode == "tp" and world > 1) else 1
     eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": args.layers}}, "maxSeqLen": 4096,
-                            "maxFrames": max(1024, F + 8), "enableFM": False, "device": local})
+                            "maxFrames": max(1024, F + 8), "enableFM": args.c3_frames > 0, "device": local,
+                            "tpSize": tp, "tpRank": rank if tp > 1 else 0})
     eng.init()
+    if tp > 1:
+        lib = nccl_lib_path()
+        uid = vdist.broadcast_bytes(vx.nccl_unique_id(lib) if rank == 0 else None)
+        vx.tp_init(eng, uid, lib)
     eng.loadRandomWeights(0)
     # A dedicated stream: the engine's kernels and the timing events share it (the
     # legacy default stream would not order with the engine's work).
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
-    utt = rank
+    utt = rank if tp == 1 else 0
     toks, a0, na = synth.prompt(utt, args.text, args.voice)
     voice = synth.voice_rows(utt, args.voice)
     eng.set_streams(3, 4, utt)
@@ -230,20 +248,49 @@ def run_b200(args):
     launches = eng.launch_count() - l0
     ms = e0.elapsed_time(e1)
     ms_max = vdist.max_over_ranks(ms)
-    frames_total = F * args.steps * world
+    frames_total = F * args.steps * (world if tp == 1 else 1)
     value = frames_total / (ms_max / 1e3)
     ms_per_step = ms_max / args.steps
 
-    # ------------------------------------------------------------------ roofline of the GEMV kernel
-    eng.rewind()
-    eng.decode(F // 2, with_fm=False)           # profile at the middle of the decode window
-    prof = eng.profile_step(reps=16)
+    # ------------------------------------------------------------------ roofline of the decode kernel
+    # One step is one launch of the persistent decode kernel (k_decode_steps) over F frames.
+    # Algorithmic bytes per launch: every frame streams all f16 weights once, reads the f16 KV
+    # of its position and the 37 embedding rows.
     peak, peak_kind = measured_peaks()
-    achieved = prof["gemv_bytes"] / (prof["gemv_ms"] / 1e3) / 1e9
-    traffic = ncu_traffic()
-    avg_pos = p0 + F / 2
-    step_bytes = args.layers * BYTES_PER_LAYER + 6144 + avg_pos * KV_BYTES_PER_POS * args.layers / 26
-    step_gbs = step_bytes * (F * args.steps) / (ms / 1e3) / 1e9
+    avg_pos = p0 + (F - 1) / 2
+    frame_bytes = (args.layers * BYTES_PER_LAYER + 6144 + 37 * 3072 * 2
+                   + (avg_pos + 1) * KV_BYTES_PER_POS * args.layers / 26) / tp
+    launch_bytes = F * frame_bytes
+    achieved = launch_bytes / (ms_per_step / 1e3) / 1e9
+    # ncu traffic of the weight stream per frame-layer (small-case capture), scaled to this
+    # launch, plus the algorithmic KV bytes (they grow with the position, not the units).
+    per_layer = ncu_traffic()
+    kv_bytes = F * (avg_pos + 1) * KV_BYTES_PER_POS * args.layers / 26 / tp
+    traffic = per_layer * args.layers * F / tp + kv_bytes if per_layer else None
+    prof = None
+    if tp == 1:
+        eng.rewind()
+        eng.decode(F // 2, with_fm=False)
+        prof = eng.profile_step(reps=8)       # the per-op kernel path, for comparison
+
+    # ------------------------------------------------------------------ C3 sample: backbone + FM per frame
+    c3 = None
+    if args.c3_frames > 0 and tp == 1:
+        eng.rewind()
+        eng.backboneStep(24)                       # AUDIO kick: frame 0's hidden state
+        eng.decode(2, with_fm=True)                # warm-up (captures the FM graph)
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        eng.decode(args.c3_frames, with_fm=True)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        c3_ms = c0.elapsed_time(c1) / args.c3_frames
+        c3 = {"frames_per_s": 1e3 / c3_ms, "ms_per_frame": c3_ms, "frames": args.c3_frames,
+              "workload": "C3: one backbone step + FM (7 Euler steps, CFG as batch 2, M=6 skinny GEMMs) + "
+                          "masked-argmax semantic code per frame, device-resident",
+              "fm_bytes_per_frame": 4961851392,
+              "frame_gbs": (frame_bytes + 4961851392) / (c3_ms / 1e3) / 1e9}
 
     # ------------------------------------------------------------------ end to end through the C ABI
     e2e_vals, h2d, d2h = [], 0, 0
@@ -263,7 +310,7 @@ def run_b200(args):
             e2e_vals.append(F / (t0.elapsed_time(t1) / 1e3))
         h2d = toks.nbytes + voice.nbytes
         d2h = codes.nbytes + normed.nbytes
-    e2e = vdist.sum_over_ranks(min(e2e_vals)) if world > 1 else e2e_vals[0]
+    e2e = vdist.sum_over_ranks(min(e2e_vals)) if (world > 1 and tp == 1) else e2e_vals[0]
 
     # ------------------------------------------------------------------ CPU baseline (rank 0, N = 1)
     cpu = None
@@ -276,18 +323,22 @@ def run_b200(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak" if tp == 1 else "strong",
             "vs_baseline": None, "dtype": "f16 weights, f32 math, f16 KV", "data": "synthetic",
             "config": {"workload": WORKLOAD, "frames_per_step": F, "prompt_positions": int(p0),
-                       "layers": args.layers, "global_batch": world, "parallelism": f"dp{world}",
+                       "layers": args.layers, "global_batch": world if tp == 1 else 1,
+                       "parallelism": f"dp{world}" if tp == 1 else f"tp{tp}",
                        "l2": "inputs larger than L2: 6.05 GB of weights streamed per frame"},
-            "roofline": {"bound": "hbm", "kernel": "k_gemv: the 104 weight-streaming GEMV launches of one "
-                                                    "step, graph-launched as a chain, CUDA events",
+            "roofline": {"bound": "hbm", "kernel": "k_decode_steps (persistent decode kernel, one launch per step)"
+                                                    if tp == 1 else "per-op kernels + NCCL (TP)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": traffic,
-                         "bytes_per_step": prof["gemv_bytes"], "gemv_ms_per_step": prof["gemv_ms"],
-                         "attn_ms_per_step": prof["attn_ms"], "full_step_ms": prof["step_ms"],
-                         "step_gbs": step_gbs, "step_frac": step_gbs / peak},
+                         "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": launch_bytes,
+                         "launch_ms": ms_per_step,
+                         "per_op_path": None if prof is None else {
+                             "gemv_chain_gbs": prof["gemv_bytes"] / (prof["gemv_ms"] / 1e3) / 1e9,
+                             "gemv_ms_per_frame": prof["gemv_ms"], "attn_ms_per_frame": prof["attn_ms"],
+                             "full_ms_per_frame": prof["step_ms"]}},
+            "c3_backbone_plus_fm": c3,
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
