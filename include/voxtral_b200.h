@@ -186,6 +186,17 @@ int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, dou
  * dimensions.  dims (nullable) receives {ctas, steps, phases, 4}. */
 int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t* dims);
 
+/* Test support for the tensor-core GEMM of the batched paths (tcgen05 / TMEM,
+ * k_gemm.cuh), which replaces matvecF16 (src/shaders.ts:21-71) when a batch of
+ * tokens shares a layer (batched prefill; the reference prefills token by token,
+ * src/engine.ts:2457-2472).  No counterpart in the reference.  Computes Y = X W^T,
+ * then Y += X W^T, for seeded random W f16 [M,K] ~ N(0, 0.02) and X f32 [N,K] ~ N(0,1),
+ * with tile width bn (64, 128 or 256) and at most max_splits K splits, and compares
+ * each pass with an f32 CUDA-core product of the same operands:
+ * out_rel_err[2] = max|Y - Yref| / max|Yref| of the two passes. */
+int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, int32_t max_splits, uint64_t seed,
+                     double* out_rel_err);
+
 /* Tensor parallelism over NCCL (batch-1 latency, heads and FFN columns
  * sharded): the unique id comes from vx_nccl_unique_id on rank 0 and is shared by
  * the host (e.g. torch.distributed).  nccl_lib: path of libnccl.so.2 (NULL: the

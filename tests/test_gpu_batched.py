@@ -1,0 +1,88 @@
+"""Tensor-core (tcgen05 / TMEM) token-batch path: the GEMM itself, and the batched
+prefill that replaces the reference's token-by-token prefill loop
+(src/engine.ts:2457-2472) against the token-by-token path and the CPU oracle."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import max_abs_rel
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2           # reference tolerance (per-tensor max-abs-rel) against the oracle
+TOL_PATHS = 1e-3     # batched vs token-by-token prefill: same f32 arithmetic up to summation order
+TOL_GEMM = 2e-5      # tensor-core GEMM (f16 W x hi/lo f16 X, f32 accumulate) vs f32 CUDA-core product
+
+
+@pytest.fixture(scope="module")
+def eng(vx):
+    e = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 1024, "maxFrames": 64,
+                          "enableFM": False})
+    e.init()
+    e.loadRandomWeights(0)
+    yield e
+    e.destroy()
+
+
+@pytest.mark.parametrize("M,N,K,bn,splits", [
+    (128, 1, 64, 128, 1),          # one tile, one K chunk, one token
+    (384, 100, 3072, 128, 1),      # ragged token tile
+    (6144, 512, 3072, 128, 8),     # QKV of a 512-token batch
+    (3072, 77, 9216, 128, 8),      # down projection, split-K
+    (256, 64, 4096, 64, 4),        # narrow tile, split-K
+    (512, 300, 1024, 256, 2),      # wide tile, two token tiles (second ragged)
+])
+def test_tc_gemm_selftest(eng, M, N, K, bn, splits):
+    e_store, e_acc = eng.selftest_gemm(M, N, K, bn=bn, max_splits=splits, seed=M + N + K)
+    assert e_store < TOL_GEMM, e_store
+    assert e_acc < TOL_GEMM, e_acc
+
+
+def _kick_layers(vx, synth, utt, T, R, batched):
+    if not batched:
+        os.environ["VX_NO_BATCHED_PREFILL"] = "1"
+    try:
+        e = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 1024, "maxFrames": 16,
+                              "enableFM": False})
+        e.init()
+    finally:
+        os.environ.pop("VX_NO_BATCHED_PREFILL", None)
+    try:
+        e.loadRandomWeights(0)
+        toks, a0, na = synth.prompt(utt, T, R)
+        e.prefill(toks, a0, na, synth.voice_rows(utt, R))
+        pos = e.position()
+        raw = e.debugBackboneLayerByLayer(24)["raw"]
+        return pos, raw
+    finally:
+        e.destroy()
+
+
+def test_batched_prefill_matches_token_by_token(vx, synth):
+    """600 prompt positions = two token batches (512 + 88): every per-layer tensor of
+    the step after prefill agrees with the token-by-token prefill."""
+    pa, a = _kick_layers(vx, synth, 7, 560, 35, batched=True)
+    pb, b = _kick_layers(vx, synth, 7, 560, 35, batched=False)
+    assert pa == pb == 600
+    for i in range(a.shape[0]):
+        assert max_abs_rel(a[i], b[i]) < TOL_PATHS, i
+
+
+def test_batched_prefill_then_decode_matches_oracle(eng, synth):
+    """Batched prefill of 545 positions, then backbone-only decode, against the oracle."""
+    toks, a0, na = synth.prompt(8, 500, 40)
+    voice = synth.voice_rows(8, 40)
+    n = 6
+    codes_in = synth.feedback_codes(9, 0, n)
+    o = oracle.Oracle(n_layers=2, max_seq=1024, with_fm=False)
+    ref = o.generate(toks, a0, na, voice, n, codes_in=codes_in, want_normed=True)
+    o.close()
+    eng.reset()
+    eng.set_streams(noise_seed=3, codes_seed=4, utt=9)
+    eng.prefill(toks, a0, na, voice)
+    assert eng.position() == len(toks)
+    eng.decode(n, with_fm=False)
+    got = eng.read_normed(0, n)
+    for f in range(n):
+        assert max_abs_rel(got[f], ref["normed"][f]) < TOL, f

@@ -5,7 +5,9 @@
 // The reference materialises the [32, seq] score matrix in global memory and
 // reads the f32 KV cache three times; here one pass reads each f16 K/V page once.
 //
-// Grid (kv_head, split, batch row), 4 warps.  A split owns a contiguous range of
+// Grid (kv_head, split, batch row), 4 warps.  A batch row is either one slot at
+// its current position or (rows_consecutive) one of a batch of consecutive
+// prompt positions of a single slot, attending causally up to its own position.  A split owns a contiguous range of
 // 64-position pages; one thread streams K and V pages (2-D TMA tiles, 128-byte
 // swizzle, double-buffered) and each warp takes 16 positions of the page.
 // The 4 query heads that share a KV head form the rows of an m16n8k16 MMA:
@@ -44,6 +46,7 @@ struct Params {
   int slot0;
   int n_splits;
   float scale;
+  int rows_consecutive;      // 1: every row is slot slot0, row m at position pos(slot0) + m (batched prefill)
 };
 
 // Byte offset of 16-byte chunk (row, col/8) inside a K or V page tile made of
@@ -63,7 +66,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x, split = blockIdx.y, row = blockIdx.z;
-  const int slot = p.slot0 + row;
+  const int slot = p.rows_consecutive ? p.slot0 : p.slot0 + row;
 
   if (threadIdx.x == 0) {
     mbar_init(&full[0], 1);
@@ -75,7 +78,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const __grid_constant_
   griddep_launch();
   griddep_wait();   // q and the K/V of the current position come from the previous kernel
 
-  const int seq = p.pos[(long long)slot * p.pos_stride] + 1;
+  const int seq = p.pos[(long long)slot * p.pos_stride] + (p.rows_consecutive ? row : 0) + 1;
   const int npages = (seq + kPage - 1) / kPage;
   const int pps = (npages + p.n_splits - 1) / p.n_splits;
   const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);

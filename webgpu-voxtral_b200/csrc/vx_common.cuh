@@ -23,6 +23,7 @@ enum DevError : int {
   kDevTimeoutRed = 3,     // epilogue / reduction slot wait expired
   kDevTimeoutDrain = 4,   // waiting for in-flight copies at exit expired
   kDevBadIndex = 5,       // an index from device memory was out of range
+  kDevTimeoutAcc = 6,     // tensor-core accumulator (tcgen05.commit) wait expired
 };
 
 __device__ int vx_dev_error;

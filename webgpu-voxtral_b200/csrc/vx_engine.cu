@@ -27,6 +27,7 @@
 
 #include "../../include/voxtral_b200.h"
 #include "k_attn.cuh"
+#include "k_gemm.cuh"
 #include "k_gemv.cuh"
 #include "k_misc.cuh"
 #include "k_step.cuh"
@@ -154,6 +155,19 @@ struct vx_handle {
   int prestage_kv = 1;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV)
   bool trace_armed = false;
 
+  // token batches on the tensor cores (k_gemm.cuh): batched prefill
+  bool use_tb = true;                  // VX_NO_BATCHED_PREFILL=1: token-by-token prefill instead
+  int tb_cap = 0;                      // rows per batch
+  struct TbLayerMaps { CUtensorMap wqkv, wo, w13, w2; };
+  std::vector<TbLayerMaps> tb_wmaps;   // per backbone layer
+  CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl
+  void* tb_buf = nullptr;
+  float *tb_h = nullptr, *tb_y = nullptr, *tb_q = nullptr, *tb_att = nullptr, *tb_part = nullptr, *tb_ws = nullptr;
+  int *tb_att_tickets = nullptr, *tb_gemm_tickets = nullptr;
+  __half *tb_hi = nullptr, *tb_lo = nullptr;
+  size_t tb_ws_floats = 0;
+  int tb_max_tiles = 0;
+
   // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
   int parts = 7;          // kPartMisc | kPartGemv | kPartAttn
   bool profiling = false;
@@ -200,6 +214,11 @@ cudaError_t gemv_attr() {
                               (int)gemv::kSmemBytes);
 }
 
+template <int BN>
+cudaError_t tc_attr() {
+  return cudaFuncSetAttribute(tc::k_gemm<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::Cfg<BN>::kSmem);
+}
+
 // Every GEMV instantiation the programs use gets its shared-memory opt-in at
 // engine creation, before any stream capture.
 int prime_kernel_attrs(vx_handle* h) {
@@ -217,6 +236,7 @@ int prime_kernel_attrs(vx_handle* h) {
   CK(gemv_attr<2, 6, 3, kStore, true>());
   CK(cudaFuncSetAttribute(attn::k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn::kSmemBytes));
   CK(cudaFuncSetAttribute(mk::k_decode_steps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(tc_attr<64>()); CK(tc_attr<128>()); CK(tc_attr<256>());
   return VX_OK;
 }
 
@@ -309,6 +329,27 @@ int make_kv_map(vx_handle* h) {
   return VX_OK;
 }
 
+// 2-D f16 tensor map, 128-byte swizzle, K innermost: `rows` rows of `inner`
+// elements, `row_bytes` apart; box = box_inner x box_rows.
+int encode_f16_2d(vx_handle* h, CUtensorMap* map, const void* base, long long inner, long long rows, long long row_bytes,
+                  int box_inner, int box_rows) {
+  static void* fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess) { fn = nullptr; return h->fail(VX_E_CUDA, "cuTensorMapEncodeTiled unavailable"); }
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = ((EncodeTiledFn)fn)(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                                   es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return h->fail(VX_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return VX_OK;
+}
+
 // -------------------------------------------------------------------- programs
 int check_device_error(vx_handle* h) {
   int e = 0;
@@ -317,8 +358,9 @@ int check_device_error(vx_handle* h) {
     int z = 0;
     cudaMemcpyToSymbol(vx::vx_dev_error, &z, sizeof(int));
     static const char* names[] = {"ok", "TMA stage wait expired", "free-stage wait expired",
-                                  "reduction slot wait expired", "drain wait expired", "index out of range"};
-    return h->fail(VX_E_DEVICE, "device-side error: %s", (e > 0 && e < 6) ? names[e] : "unknown");
+                                  "reduction slot wait expired", "drain wait expired", "index out of range",
+                                  "tensor-core accumulator wait expired"};
+    return h->fail(VX_E_DEVICE, "device-side error: %s", (e > 0 && e < 7) ? names[e] : "unknown");
   }
   return VX_OK;
 }
@@ -571,6 +613,127 @@ int slot_update(vx_handle* h, int slot, const SlotUpdate& u) {
   k_slot_update<<<1, 32, 0, h->stream>>>(h->slots, slot, u);
   h->launches++;
   CK(cudaGetLastError());
+  return VX_OK;
+}
+
+// ---------------------------------------------------------------- token batches (k_gemm.cuh)
+// Y[N, M] (=|+=) X[N, K] W[M, K]^T on the tensor cores.  Split-K fills the SMs
+// when the output has fewer tiles than SMs (at most `max_splits` splits).
+template <int BN>
+int run_tc_gemm(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo, float* y,
+                long long ldy, int M, int N, int K, int accumulate, int max_splits = 8) {
+  if (N < 1 || M < 1 || K < tc::kBK || K % tc::kBK) return h->fail(VX_E_INVALID, "tensor-core GEMM shape %dx%dx%d", M, N, K);
+  const int n_tiles = (N + BN - 1) / BN, m_tiles = (M + tc::kBM - 1) / tc::kBM;
+  const int chunks = K / tc::kBK;
+  const int tiles = n_tiles * m_tiles;
+  int splits = 1;
+  if (tiles < h->num_sms) splits = std::min({chunks, max_splits, (h->num_sms + tiles - 1) / tiles});
+  while (splits > 1 && ((size_t)tiles * splits * BN * tc::kBM > h->tb_ws_floats || tiles > h->tb_max_tiles)) --splits;
+  const int cps = (chunks + splits - 1) / splits;
+  splits = (chunks + cps - 1) / cps;
+  tc::Params p{y, ldy, h->tb_ws, h->tb_gemm_tickets, M, N, K, cps, accumulate};
+  CK(launch(h, tc::k_gemm<BN>, dim3(n_tiles, m_tiles, splits), dim3(tc::kThreads), tc::Cfg<BN>::kSmem, w, xhi, xlo, p));
+  return VX_OK;
+}
+
+// The N prompt positions of a slot through the backbone as token batches of up
+// to tb_cap rows: every projection is one tensor-core GEMM over the batch
+// instead of N weight-streaming steps (the reference runs one backboneStep per
+// prompt token, src/engine.ts:2457-2472).  Leaves the slot as the token-by-token
+// prefill does: K/V of every position cached, position advanced by N, the last
+// position's final-norm state in `normed` and its residual stream in `h`.
+int prefill_tb(vx_handle* h, int slot, int n) {
+  const int D = h->D;
+  int rc;
+  tc::TokRows tr{&h->slots[0].pos, kPosStride, 0, slot};
+  gemv::KvGeom kg{h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV, kPage};
+  const float eps = h->cfg.norm_eps;
+  int nc = 0;
+  for (int c0 = 0; c0 < n; c0 += h->tb_cap) {
+    nc = std::min(h->tb_cap, n - c0);
+    tc::TbEmbedParams ep{h->tok_emb, h->V, h->prompt, h->voice, h->cfg.max_seq_len, h->cfg.max_voice_rows, D, h->tb_h, tr};
+    CK(launch(h, tc::k_tb_embed, dim3(nc), dim3(256), 0, ep));
+    for (int l = 0; l < h->L; ++l) {
+      const LayerW& W = h->layers[l];
+      const vx_handle::TbLayerMaps& mp = h->tb_wmaps[l];
+      CK(launch(h, tc::k_tb_norm_split, dim3(nc), dim3(256), 0, (const float*)h->tb_h, (const __half*)W.attn_norm, D,
+                eps, h->tb_hi, h->tb_lo));
+      if ((rc = run_tc_gemm<128>(h, mp.wqkv, h->tb_xhi[0], h->tb_xlo[0], h->tb_y, h->QKVD, h->QKVD, nc, D, 0))) return rc;
+      tc::RopeKvParams rp{h->tb_y, h->tb_q, h->QD, h->KVD, nc, h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV,
+                          kPage, l, h->rope_freq, tr};
+      CK(launch(h, tc::k_tb_rope_kv, dim3(nc), dim3(256), 0, rp));
+      attn::Params ap{};
+      ap.q = h->tb_q; ap.ldq = h->QD; ap.out = h->tb_att; ap.ldo = h->QD;
+      ap.part = h->tb_part; ap.tickets = h->tb_att_tickets;
+      ap.kv = kg; ap.layer = l; ap.pos = &h->slots[0].pos; ap.pos_stride = kPosStride; ap.slot0 = slot;
+      ap.n_splits = 1; ap.scale = 1.0f / sqrtf((float)h->HD); ap.rows_consecutive = 1;
+      CK(launch(h, attn::k_attn_decode, dim3(h->NKV, 1, nc), dim3(attn::kThreads), attn::kSmemBytes, h->kv_map, ap));
+      const long long na = (long long)nc * h->QD;
+      CK(launch(h, tc::k_tb_split, dim3((unsigned)std::min<long long>((na + 255) / 256, 4L * h->num_sms)), dim3(256), 0,
+                (const float*)h->tb_att, na, h->tb_hi, h->tb_lo));
+      if ((rc = run_tc_gemm<128>(h, mp.wo, h->tb_xhi[1], h->tb_xlo[1], h->tb_h, D, D, nc, h->QD, 1))) return rc;
+      CK(launch(h, tc::k_tb_norm_split, dim3(nc), dim3(256), 0, (const float*)h->tb_h, (const __half*)W.ffn_norm, D,
+                eps, h->tb_hi, h->tb_lo));
+      if ((rc = run_tc_gemm<128>(h, mp.w13, h->tb_xhi[0], h->tb_xlo[0], h->tb_y, 2LL * h->Fl, 2 * h->Fl, nc, D, 0)))
+        return rc;
+      const long long ng = (long long)nc * h->Fl;
+      CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
+                dim3(256), 0, (const float*)h->tb_y, nc, h->Fl, h->tb_hi, h->tb_lo));
+      if ((rc = run_tc_gemm<128>(h, mp.w2, h->tb_xhi[2], h->tb_xlo[2], h->tb_h, D, D, nc, h->Fl, 1))) return rc;
+    }
+    CK(launch(h, tc::k_tb_advance, dim3(1), dim3(32), 0, &h->slots[slot].pos, nc));
+  }
+  // last position: final norm into `normed`, residual stream into `h`
+  FinalNormParams fp{};
+  fp.h = h->tb_h + (long long)(nc - 1) * D; fp.w = h->final_norm; fp.out = h->normed + (long long)slot * D; fp.D = D;
+  fp.eps = eps;
+  CK(launch(h, k_final_norm, dim3(1), dim3(256), 0, fp));
+  CK(cudaMemcpyAsync(h->h + (long long)slot * D, fp.h, (size_t)D * 4, cudaMemcpyDeviceToDevice, h->stream));
+  return VX_OK;
+}
+
+// Buffers and tensor maps of the token-batch path (tp == 1).
+int setup_tb(vx_handle* h) {
+  const long long D = h->D;
+  h->tb_cap = 512;
+  const long long cap = h->tb_cap;
+  const long long kmax = std::max<long long>({D, (long long)h->QD, (long long)h->Fl});
+  const long long ymax = std::max<long long>(h->QKVD, 2LL * h->Fl);
+  h->tb_ws_floats = (size_t)8 << 20;
+  h->tb_max_tiles = 4096;
+  size_t bytes = 0;
+  auto add = [&](size_t b) { bytes += (b + 255) & ~size_t(255); };
+  add(cap * D * 4); add(cap * ymax * 4); add(cap * h->QD * 4); add(cap * h->QD * 4);
+  add(cap * h->NKV * attn::kGqa * attn::kPartStride * 4); add(h->tb_ws_floats * 4);
+  add(cap * h->NKV * 4); add((size_t)h->tb_max_tiles * 4); add(cap * kmax * 2); add(cap * kmax * 2);
+  if (cudaMalloc(&h->tb_buf, bytes) != cudaSuccess) return h->fail(VX_E_NOMEM, "token-batch buffers (%.1f MB)", bytes / 1e6);
+  CK(cudaMemset(h->tb_buf, 0, bytes));
+  uint8_t* cur = (uint8_t*)h->tb_buf;
+  h->tb_h = (float*)carve(cur, cap * D * 4);
+  h->tb_y = (float*)carve(cur, cap * ymax * 4);
+  h->tb_q = (float*)carve(cur, cap * h->QD * 4);
+  h->tb_att = (float*)carve(cur, cap * h->QD * 4);
+  h->tb_part = (float*)carve(cur, cap * h->NKV * attn::kGqa * attn::kPartStride * 4);
+  h->tb_ws = (float*)carve(cur, h->tb_ws_floats * 4);
+  h->tb_att_tickets = (int*)carve(cur, cap * h->NKV * 4);
+  h->tb_gemm_tickets = (int*)carve(cur, (size_t)h->tb_max_tiles * 4);
+  h->tb_hi = (__half*)carve(cur, cap * kmax * 2);
+  h->tb_lo = (__half*)carve(cur, cap * kmax * 2);
+  int rc;
+  const long long ks[3] = {D, (long long)h->QD, (long long)h->Fl};
+  for (int i = 0; i < 3; ++i) {
+    if ((rc = encode_f16_2d(h, &h->tb_xhi[i], h->tb_hi, ks[i], cap, ks[i] * 2, tc::kBK, 128))) return rc;
+    if ((rc = encode_f16_2d(h, &h->tb_xlo[i], h->tb_lo, ks[i], cap, ks[i] * 2, tc::kBK, 128))) return rc;
+  }
+  h->tb_wmaps.resize(h->L);
+  for (int l = 0; l < h->L; ++l) {
+    const LayerW& W = h->layers[l];
+    vx_handle::TbLayerMaps& m = h->tb_wmaps[l];
+    if ((rc = encode_f16_2d(h, &m.wqkv, W.wqkv, D, h->QKVD, D * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.wo, W.wo, h->QD, D, h->QD * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.w13, W.w13, D, 2LL * h->Fl, D * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.w2, W.w2, h->Fl, D, (long long)h->Fl * 2, tc::kBK, tc::kBM))) return rc;
+  }
   return VX_OK;
 }
 
@@ -846,6 +1009,11 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     const char* e = getenv("VX_NO_MEGAKERNEL");
     h->use_mk = coop && h->tp == 1 && !(e && e[0] == '1');
   }
+  {
+    const char* e = getenv("VX_NO_BATCHED_PREFILL");
+    h->use_tb = h->tp == 1 && !(e && e[0] == '1');
+    if (h->use_tb && (rc = setup_tb(h))) { *out = h; return rc; }
+  }
   *out = h;
   return VX_OK;
 }
@@ -862,10 +1030,71 @@ void vx_destroy(vx_handle* h) {
   if (h->d_layers) cudaFree(h->d_layers);
   if (h->d_trace) cudaFree(h->d_trace);
   if (h->kv_pool) cudaFree(h->kv_pool);
+  if (h->tb_buf) cudaFree(h->tb_buf);
   if (h->rope_freq) cudaFree(h->rope_freq);   // base of the activation block
   if (h->pinned) cudaFreeHost(h->pinned);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   delete h;
+}
+
+// Test support, no counterpart in the reference: the tensor-core GEMM of the
+// batched paths against an f32 CUDA-core product of the same seeded operands.
+int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, int32_t max_splits, uint64_t seed,
+                     double* out_rel_err) {
+  if (!h || !out_rel_err) return VX_E_INVALID;
+  if (!h->use_tb) return h->fail(VX_E_STATE, "token-batch path is off (tp > 1 or VX_NO_BATCHED_PREFILL)");
+  if (M < 1 || N < 1 || K < 64 || K % 64 || !(bn == 64 || bn == 128 || bn == 256) || max_splits < 1 ||
+      (long long)M * K > (1LL << 28) || (long long)N * K > (1LL << 26) || (long long)N * M > (1LL << 26))
+    return h->fail(VX_E_INVALID, "selftest shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
+  CK(cudaSetDevice(h->dev));
+  __half *W = nullptr, *hi = nullptr, *lo = nullptr;
+  float *X = nullptr, *Y = nullptr, *R = nullptr;
+  int rc = VX_OK;
+  const size_t nw = (size_t)M * K, nx = (size_t)N * K, ny = (size_t)N * M;
+  if (cudaMalloc(&W, nw * 2) != cudaSuccess || cudaMalloc(&hi, nx * 2) != cudaSuccess ||
+      cudaMalloc(&lo, nx * 2) != cudaSuccess || cudaMalloc(&X, nx * 4) != cudaSuccess ||
+      cudaMalloc(&Y, ny * 4) != cudaSuccess || cudaMalloc(&R, ny * 4) != cudaSuccess)
+    rc = h->fail(VX_E_NOMEM, "selftest buffers");
+  CUtensorMap wm, xh, xl;
+  if (!rc) rc = encode_f16_2d(h, &wm, W, K, M, (long long)K * 2, tc::kBK, tc::kBM);
+  if (!rc) rc = encode_f16_2d(h, &xh, hi, K, N, (long long)K * 2, tc::kBK, bn);
+  if (!rc) rc = encode_f16_2d(h, &xl, lo, K, N, (long long)K * 2, tc::kBK, bn);
+  std::vector<float> y(ny), r(ny);
+  if (!rc) {
+    const uint64_t key = vx_stream_key(seed, 77);
+    if (launch(h, tc::k_selftest_fill, dim3(4 * h->num_sms), dim3(256), 0, W, (long long)nw, X, (long long)nx, key) !=
+            cudaSuccess ||
+        launch(h, tc::k_tb_split, dim3(4 * h->num_sms), dim3(256), 0, (const float*)X, (long long)nx, hi, lo) !=
+            cudaSuccess)
+      rc = h->fail(VX_E_CUDA, "selftest fill");
+  }
+  for (int pass = 0; pass < 2 && !rc; ++pass) {
+    if (bn == 64) rc = run_tc_gemm<64>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
+    else if (bn == 128) rc = run_tc_gemm<128>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
+    else rc = run_tc_gemm<256>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
+    if (!rc && pass == 0) {
+      tc::k_ref_gemm<<<dim3((M + 127) / 128, N), 128, 0, h->stream>>>(W, X, M, N, K, R);
+      if (cudaGetLastError() != cudaSuccess) rc = h->fail(VX_E_CUDA, "reference GEMM launch");
+    }
+    if (!rc && cudaMemcpyAsync(y.data(), Y, ny * 4, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess)
+      rc = h->fail(VX_E_CUDA, "selftest copy");
+    if (!rc && pass == 0 && cudaMemcpyAsync(r.data(), R, ny * 4, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess)
+      rc = h->fail(VX_E_CUDA, "selftest copy");
+    if (!rc) rc = finish(h);
+    if (!rc) {
+      double emax = 0, rmax = 0;
+      const double f = pass + 1.0;
+      for (size_t i = 0; i < ny; ++i) {
+        emax = std::max(emax, std::fabs((double)y[i] - f * r[i]));
+        rmax = std::max(rmax, std::fabs(f * r[i]));
+      }
+      out_rel_err[pass] = rmax > 0 ? emax / rmax : emax;
+    }
+  }
+  cudaStreamSynchronize(h->stream);
+  for (void* ptr : {(void*)W, (void*)hi, (void*)lo, (void*)X, (void*)Y, (void*)R})
+    if (ptr) cudaFree(ptr);
+  return rc;
 }
 
 int vx_set_stream(vx_handle* h, void* stream) {
@@ -1011,7 +1240,9 @@ int vx_prefill(vx_handle* h, int32_t slot, const int32_t* tokens, int32_t n, int
   u.set_mode = 1; u.mode = kEmbPrompt; u.token = 0;
   u.set_prompt_len = 1; u.prompt_len = p0 + n;
   if ((rc = slot_update(h, slot, u))) return rc;
-  if (h->use_mk) {
+  if (h->use_tb) {
+    if ((rc = prefill_tb(h, slot, n))) return rc;
+  } else if (h->use_mk) {
     if ((rc = launch_steps(h, slot, n, kEmbPrompt, 0, kEmbPrompt, false, false))) return rc;
   } else {
     for (int i = 0; i < n; ++i)

@@ -102,6 +102,8 @@ def load_library():
         "vx_profile_step": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p,
                                            ctypes.POINTER(ctypes.c_double)]),
         "vx_trace": (ctypes.c_int, [H, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, _i32p]),
+        "vx_selftest_gemm": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_uint64, ctypes.POINTER(ctypes.c_double)]),
         "vx_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p, _u8p]),
         "vx_tp_init": (ctypes.c_int, [H, ctypes.c_char_p, _u8p]),
     }
@@ -265,6 +267,12 @@ class VoxtralEngine:
         self._check(load_library().vx_profile_step(self._h, slot, reps, _p(ms, _f32p), ctypes.byref(by)))
         return {"step_ms": float(ms[0]), "gemv_ms": float(ms[1]), "attn_ms": float(ms[2]),
                 "gemv_bytes": float(by.value)}
+
+    def selftest_gemm(self, M: int, N: int, K: int, bn: int = 128, max_splits: int = 8, seed: int = 0):
+        """Tensor-core GEMM vs an f32 CUDA-core product: (rel err of Y = XW^T, rel err of Y += XW^T)."""
+        err = (ctypes.c_double * 2)()
+        self._check(load_library().vx_selftest_gemm(self._h, M, N, K, bn, max_splits, seed, err))
+        return float(err[0]), float(err[1])
 
     def trace_arm(self):
         """Record phase timestamps of the next persistent-kernel launch (first 2 steps)."""
