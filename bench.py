@@ -221,6 +221,24 @@ def run_b200(args):
     eng.checkpoint()
     p0 = eng.position()
 
+    # time-to-first-frame: the batched prefill of the prompt (tensor-core GEMMs)
+    pf_ms = []
+    for _ in range(3):
+        eng.reset()
+        torch.cuda.synchronize()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record(stream)
+        eng.prefill(toks, a0, na, voice)
+        q1.record(stream)
+        torch.cuda.synchronize()
+        pf_ms.append(q0.elapsed_time(q1))
+    eng.checkpoint()
+    prefill = {"positions": int(p0), "ms": min(pf_ms),
+               "gemm_tflops": 2.0 * p0 * args.layers * (BYTES_PER_LAYER / 2) / (min(pf_ms) / 1e3) / 1e12,
+               "note": "batched prefill: every projection one tcgen05 GEMM over <=512 positions, "
+                       "activations as an f16 hi/lo pair (2 MMAs per K step; TFLOP/s counts 2 flops per weight "
+                       "per position once)"}
+
     def step():
         eng.rewind()
         eng.decode(F, with_fm=False)
@@ -339,6 +357,7 @@ def run_b200(args):
                              "gemv_ms_per_frame": prof["gemv_ms"], "attn_ms_per_frame": prof["attn_ms"],
                              "full_ms_per_frame": prof["step_ms"]}},
             "c3_backbone_plus_fm": c3,
+            "prefill": prefill,
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
