@@ -146,6 +146,15 @@ int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out);
  * read results with vx_read_codes / vx_read_normed after vx_synchronize. */
 int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm);
 
+/* Batched backbone-only decode: n_frames frames of slots [slot0, slot0 + n_slots) in
+ * lockstep, each slot at its own position with its own synthetic feedback codes
+ * (vx_set_streams), exactly as vx_decode(slot, n_frames, 0) would produce them one slot
+ * at a time (frame 0 of a slot is the AUDIO kick).  The reference decodes one utterance
+ * per engine (generate() frame loop, src/engine.ts:2498-2585); here every projection of
+ * a step is one tensor-core GEMM over the n_slots rows, so the weights stream once per
+ * step for all slots.  Needs tp_size 1; n_slots <= 512. */
+int vx_decode_batch(vx_handle* h, int32_t slot0, int32_t n_slots, int32_t n_frames);
+
 /* Seeds of the slot's synthetic streams (FM noise, backbone-only feedback codes);
  * `utt` selects the utterance stream of vx_rng.h. */
 int vx_set_streams(vx_handle* h, int32_t slot, uint64_t noise_seed, uint64_t codes_seed, int32_t utt);

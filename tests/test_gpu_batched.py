@@ -86,3 +86,65 @@ def test_batched_prefill_then_decode_matches_oracle(eng, synth):
     got = eng.read_normed(0, n)
     for f in range(n):
         assert max_abs_rel(got[f], ref["normed"][f]) < TOL, f
+
+
+def _prefill_slots(e, synth, n, base_utt=20):
+    """Slots 0..n-1 hold different prompts (different lengths, so different positions)."""
+    for s in range(n):
+        u = base_utt + s
+        toks, a0, na = synth.prompt(u, 40 + 13 * s, 6 + s)
+        e.reset(slot=s)
+        e.set_streams(noise_seed=3, codes_seed=4, utt=u, slot=s)
+        e.prefill(toks, a0, na, synth.voice_rows(u, 6 + s), slot=s)
+
+
+def test_batched_decode_matches_per_slot_decode(vx, synth):
+    """vx_decode_batch over 8 slots (tensor-core GEMMs, one row per slot) reproduces the
+    batch-1 decode of each slot: same feedback codes, same normed states."""
+    n, frames = 8, 10
+    cfg = {"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 1024, "maxFrames": 64, "enableFM": False,
+           "maxSlots": n}
+    a = vx.VoxtralEngine(cfg)
+    a.init()
+    a.loadRandomWeights(0)
+    try:
+        _prefill_slots(a, synth, n)
+        a.decode_batch(frames, n)
+        got = [a.read_normed(0, frames, slot=s) for s in range(n)]
+        got_codes = [a.read_codes(0, frames - 1, slot=s) for s in range(n)]
+        pos = [a.position(s) for s in range(n)]
+        _prefill_slots(a, synth, n)
+        for s in range(n):
+            a.decode(frames, with_fm=False, slot=s)
+        for s in range(n):
+            ref = a.read_normed(0, frames, slot=s)
+            assert np.array_equal(got_codes[s], a.read_codes(0, frames - 1, slot=s)), s
+            assert pos[s] == a.position(s), s
+            for f in range(frames):
+                assert max_abs_rel(got[s][f], ref[f]) < TOL_PATHS, (s, f)
+    finally:
+        a.destroy()
+
+
+def test_batched_decode_matches_oracle(vx, synth):
+    """One slot of a batched decode against the CPU oracle (reference tolerance)."""
+    n, frames = 4, 6
+    e = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 1024, "maxFrames": 64,
+                          "enableFM": False, "maxSlots": n})
+    e.init()
+    e.loadRandomWeights(0)
+    try:
+        _prefill_slots(e, synth, n, base_utt=30)
+        e.decode_batch(frames, n)
+        s = 2
+        u = 30 + s
+        toks, a0, na = synth.prompt(u, 40 + 13 * s, 6 + s)
+        o = oracle.Oracle(n_layers=2, max_seq=1024, with_fm=False)
+        ref = o.generate(toks, a0, na, synth.voice_rows(u, 6 + s), frames,
+                         codes_in=synth.feedback_codes(u, 0, frames), want_normed=True)
+        o.close()
+        got = e.read_normed(0, frames, slot=s)
+        for f in range(frames):
+            assert max_abs_rel(got[f], ref["normed"][f]) < TOL, f
+    finally:
+        e.destroy()

@@ -47,6 +47,8 @@ struct Params {
   int n_splits;
   float scale;
   int rows_consecutive;      // 1: every row is slot slot0, row m at position pos(slot0) + m (batched prefill)
+  __half* out_hi;            // nullable: out also as an f16 hi / lo pair [rows][ldo] (tensor-core GEMM operand)
+  __half* out_lo;
 };
 
 // Byte offset of 16-byte chunk (row, col/8) inside a K or V page tile made of
@@ -287,7 +289,13 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const __grid_constant_
     float O = 0.f;
 #pragma unroll 8
     for (int sp = 0; sp < n_used; ++sp) O += __ldcg(pb + sp * kGqa * kPartStride + h * kPartStride + 2 + d) * s_w[sp][h];
-    p.out[(long long)row * p.ldo + (long long)(kvh * kGqa + h) * kHd + d] = O;
+    const long long oi = (long long)row * p.ldo + (long long)(kvh * kGqa + h) * kHd + d;
+    p.out[oi] = O;
+    if (p.out_hi) {
+      const __half hh = __float2half_rn(O);
+      p.out_hi[oi] = hh;
+      p.out_lo[oi] = __float2half_rn(O - __half2float(hh));
+    }
   }
   if (threadIdx.x == 0) p.tickets[row * p.kv.n_kv + kvh] = 0;
 }

@@ -25,9 +25,9 @@
 //   warp 2         allocates / frees the TMEM accumulator (BN columns);
 //   all 4 warps    epilogue: tcgen05.ld (warp w reads TMEM lanes 32w..32w+31),
 //                  stores Y[n, m] with m along the lanes (coalesced).
-// Split-K: every split writes its f32 partial tile to a workspace; the last CTA
-// of the tile (atomic ticket) sums the partials in split order 0..S-1, so the
-// result does not depend on which CTA finishes last.
+// Split-K: every split writes its f32 partial tile to a workspace and
+// k_splitk_reduce (the next launch) sums the partials in split order 0..S-1 over
+// the whole output at once, so the result does not depend on CTA timing.
 #pragma once
 #include "vx_common.cuh"
 #include "vx_rng.h"
@@ -56,7 +56,6 @@ struct Params {
   float* y;              // Y[n * ldy + m]
   long long ldy;
   float* ws;             // split-K partials [m_tiles * n_tiles][splits][BN][kBM]
-  int* tickets;          // [m_tiles * n_tiles], zero between launches
   int M, N, K;
   int chunks_per_split;  // K chunks (kBK each) per split
   int accumulate;        // 0: Y = acc, 1: Y += acc (residual)
@@ -124,8 +123,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
   uint64_t* empty = full + C::kStages;
   uint64_t* accb = empty + C::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
-  __shared__ int s_last;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z, splits = gridDim.z;
   const int m0 = m_tile * kBM, n0 = n_tile * BN;
@@ -216,25 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
 #pragma unroll
       for (int j = 0; j < 16; ++j) wst[(long long)split * BN * kBM + (c + j) * kBM + row] = live ? v[j] : 0.f;
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = (atomicAdd(&p.tickets[tile], 1) == splits - 1);
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      if (m < p.M) {
-#pragma unroll 1
-        for (int c = 0; c < BN; ++c) {
-          const int n = n0 + c;
-          if (n >= p.N) break;
-          float acc = 0.f;
-          for (int s = 0; s < splits; ++s) acc += __ldcg(wst + (long long)s * BN * kBM + c * kBM + row);
-          float* yp = p.y + (long long)n * p.ldy + m;
-          *yp = p.accumulate ? *yp + acc : acc;
-        }
-      }
-      if (threadIdx.x == 0) p.tickets[tile] = 0;
-    }
   }
 
   // ---- teardown: every tcgen05.ld has completed (wait::ld above)
@@ -246,19 +224,49 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
   }
 }
 
+// Sum of the split-K partials of k_gemm, in split order, into Y (= or +=).  One
+// thread per 4 consecutive output rows m of one token n (float4 along m).
+struct ReduceParams {
+  const float* ws;
+  float* y;
+  long long ldy;
+  int M, N, splits, n_tiles, bn, accumulate;
+};
+__global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ ReduceParams p) {
+  griddep_launch();
+  griddep_wait();
+  const long long total = (long long)p.N * (p.M / 4);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / (p.M / 4)), m = (int)(i % (p.M / 4)) * 4;
+    const int tile = (m / kBM) * p.n_tiles + n / p.bn;
+    const float* src = p.ws + ((long long)tile * p.splits * p.bn + n % p.bn) * kBM + m % kBM;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < p.splits; ++s) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (long long)s * p.bn * kBM));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    float4* yp = reinterpret_cast<float4*>(p.y + (long long)n * p.ldy + m);
+    if (p.accumulate) {
+      const float4 y = *yp;
+      acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
+    }
+    *yp = acc;
+  }
+}
+
 // ---------------------------------------------------------------- token batches
 // Which (slot, position) each activation row belongs to.
 //   mode 0: the N consecutive prompt positions of slot `slot`, starting at the
 //           slot's current position (batched prefill);
-//   mode 1: row r is slot r at its current position (batched decode).
+//   mode 1: row r is slot `slot` + r at its current position (batched decode).
 struct TokRows {
   const int32_t* pos;   // &SlotState[0].pos
   int pos_stride;       // ints between consecutive slots' states
   int mode, slot;
 };
-__device__ __forceinline__ int tok_slot(const TokRows& t, int r) { return t.mode == 0 ? t.slot : r; }
+__device__ __forceinline__ int tok_slot(const TokRows& t, int r) { return t.mode == 0 ? t.slot : t.slot + r; }
 __device__ __forceinline__ int tok_pos(const TokRows& t, int r) {
-  return t.mode == 0 ? t.pos[(long long)t.slot * t.pos_stride] + r : t.pos[(long long)r * t.pos_stride];
+  return t.mode == 0 ? t.pos[(long long)t.slot * t.pos_stride] + r : t.pos[(long long)(t.slot + r) * t.pos_stride];
 }
 
 __device__ __forceinline__ void split_store(__half* hi, __half* lo, long long i, float x) {
@@ -357,6 +365,118 @@ __global__ void __launch_bounds__(256) k_tb_rope_kv(const __grid_constant__ Rope
       const long long prow =
           ((((long long)page * p.n_layers + p.layer) * 2 + kv) * p.n_kv + head) * p.page_size + pos % p.page_size;
       p.pool[prow * 128 + d] = __float2half_rn(out);
+    }
+  }
+}
+
+// Per-row epilogue of a token-batch GEMM, one CTA (256 threads) per activation
+// row n: sums the split-K partials of the row in split order (splits == 0: the
+// GEMM wrote its result to Y itself) and then
+//   kRowResidNorm: h[n] += partials; x' = RMSNorm(h[n]) * w -> hi/lo operand pair
+//                  of the next GEMM (norm_w null: no operand output);
+//   kRowQkv:       RoPE on the q / k parts, q -> Q[n], K/V appended to the paged
+//                  cache at the row's position (the math of k_tb_rope_kv).
+enum RowMode { kRowResidNorm = 0, kRowQkv = 1 };
+struct RowParams {
+  const float* ws;
+  int splits, n_tiles, bn;   // partial layout of k_gemm: [tile][split][bn][kBM]
+  float* y;                  // h [N][ldy] (kRowResidNorm) or the QKV rows (kRowQkv, splits == 0)
+  long long ldy;
+  int M;
+  int mode;
+  const __half* norm_w;
+  float eps;
+  __half *hi, *lo;           // [N][M]
+  RopeKvParams rope;         // kRowQkv (rope.qkv unused)
+};
+template <int V4>   // float4 groups per thread: M = 4 * 256 * V4
+__global__ void __launch_bounds__(256) k_tb_row(const __grid_constant__ RowParams p) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float sh[8];
+  const int n = blockIdx.x;
+  float4 v[V4];
+#pragma unroll
+  for (int u = 0; u < V4; ++u) {
+    const int m = (threadIdx.x + 256 * u) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p.splits == 0) {
+      acc = *reinterpret_cast<const float4*>(p.y + (long long)n * p.ldy + m);
+    } else {
+      const int tile = (m / kBM) * p.n_tiles + n / p.bn;
+      const float* src = p.ws + ((long long)tile * p.splits * p.bn + n % p.bn) * kBM + m % kBM;
+      for (int s = 0; s < p.splits; ++s) {
+        const float4 w = __ldcg(reinterpret_cast<const float4*>(src + (long long)s * p.bn * kBM));
+        acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
+      }
+      if (p.mode == kRowResidNorm) {
+        const float4 h = *reinterpret_cast<const float4*>(p.y + (long long)n * p.ldy + m);
+        acc = make_float4(h.x + acc.x, h.y + acc.y, h.z + acc.z, h.w + acc.w);
+        *reinterpret_cast<float4*>(p.y + (long long)n * p.ldy + m) = acc;
+      }
+    }
+    v[u] = acc;
+  }
+  if (p.mode == kRowResidNorm) {
+    if (!p.norm_w) return;
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < V4; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += sh[i];
+    const float rms = 1.0f / sqrtf(tot / (float)p.M + p.eps);
+#pragma unroll
+    for (int u = 0; u < V4; ++u) {
+      const int m = (threadIdx.x + 256 * u) * 4;
+      const __half2* w2 = reinterpret_cast<const __half2*>(p.norm_w + m);
+      const float2 wa = __half22float2(w2[0]), wb = __half22float2(w2[1]);
+      const long long o = (long long)n * p.M + m;
+      split_store(p.hi, p.lo, o + 0, v[u].x * rms * wa.x);
+      split_store(p.hi, p.lo, o + 1, v[u].y * rms * wa.y);
+      split_store(p.hi, p.lo, o + 2, v[u].z * rms * wb.x);
+      split_store(p.hi, p.lo, o + 3, v[u].w * rms * wb.y);
+    }
+    return;
+  }
+  // kRowQkv: RoPE pairs are (m, m+1) inside each float4
+  const RopeKvParams& r = p.rope;
+  const int slot = tok_slot(r.rows, n), pos = tok_pos(r.rows, n);
+  const int lp = pos / r.page_size;
+  const bool page_ok = pos >= 0 && lp < r.max_pages;
+  if (!page_ok && threadIdx.x == 0) set_error(kDevBadIndex);
+  const int page = page_ok ? r.page_table[(long long)slot * r.max_pages + lp] : 0;
+#pragma unroll
+  for (int u = 0; u < V4; ++u) {
+    const int m = (threadIdx.x + 256 * u) * 4;
+    float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+    if (m < r.q_dim + r.kv_dim) {
+#pragma unroll
+      for (int q = 0; q < 4; q += 2) {
+        const int pair = ((m + q) & 127) >> 1;
+        const float ang = (float)pos * r.rope_freq[pair];
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        const float x0 = e[q], x1 = e[q + 1];
+        e[q] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        e[q + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+      }
+    }
+    if (m < r.q_dim) {
+      *reinterpret_cast<float4*>(r.q + (long long)n * r.q_dim + m) = make_float4(e[0], e[1], e[2], e[3]);
+    } else if (page_ok && m < r.q_dim + 2 * r.kv_dim) {
+      const int kvr = m - r.q_dim;
+      const int kv = kvr >= r.kv_dim ? 1 : 0;
+      const int rr = kvr - kv * r.kv_dim;
+      const int head = rr >> 7, d = rr & 127;
+      const long long prow =
+          ((((long long)page * r.n_layers + r.layer) * 2 + kv) * r.n_kv + head) * r.page_size + pos % r.page_size;
+      __half2* dst = reinterpret_cast<__half2*>(r.pool + prow * 128 + d);
+      dst[0] = __floats2half2_rn(e[0], e[1]);
+      dst[1] = __floats2half2_rn(e[2], e[3]);
     }
   }
 }

@@ -156,17 +156,20 @@ struct vx_handle {
   bool trace_armed = false;
 
   // token batches on the tensor cores (k_gemm.cuh): batched prefill
-  bool use_tb = true;                  // VX_NO_BATCHED_PREFILL=1: token-by-token prefill instead
+  bool use_tb = true;                  // VX_NO_BATCHED_PREFILL=1: no token-batch path (token-by-token prefill)
+  bool prefill_tokenwise = false;      // VX_PREFILL_TOKENWISE=1: token-by-token prefill, batch path kept
   int tb_cap = 0;                      // rows per batch
   struct TbLayerMaps { CUtensorMap wqkv, wo, w13, w2; };
   std::vector<TbLayerMaps> tb_wmaps;   // per backbone layer
-  CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl
+  CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl (128-row boxes)
+  CUtensorMap tb_xhi64[3], tb_xlo64[3];  // the same with 64-row boxes (batches of <= 64 rows)
+  std::unordered_map<long long, G> g_batch;   // batched decode step graphs, key (slot0, n)
   void* tb_buf = nullptr;
   float *tb_h = nullptr, *tb_y = nullptr, *tb_q = nullptr, *tb_att = nullptr, *tb_part = nullptr, *tb_ws = nullptr;
-  int *tb_att_tickets = nullptr, *tb_gemm_tickets = nullptr;
+  int* tb_att_tickets = nullptr;
   __half *tb_hi = nullptr, *tb_lo = nullptr;
   size_t tb_ws_floats = 0;
-  int tb_max_tiles = 0;
+  int tb_attn_splits = 2;              // attention splits per (slot, KV head) in batched decode (VX_BATCH_ATTN_SPLITS)
 
   // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
   int parts = 7;          // kPartMisc | kPartGemv | kPartAttn
@@ -618,21 +621,96 @@ int slot_update(vx_handle* h, int slot, const SlotUpdate& u) {
 
 // ---------------------------------------------------------------- token batches (k_gemm.cuh)
 // Y[N, M] (=|+=) X[N, K] W[M, K]^T on the tensor cores.  Split-K fills the SMs
-// when the output has fewer tiles than SMs (at most `max_splits` splits).
+// when the output has fewer tiles than SMs: floor(SMs / tiles) splits (at most
+// `max_splits`), so that the CTAs form one whole wave.
 template <int BN>
 int run_tc_gemm(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo, float* y,
-                long long ldy, int M, int N, int K, int accumulate, int max_splits = 8) {
+                long long ldy, int M, int N, int K, int accumulate, int max_splits = 8, int* splits_out = nullptr) {
   if (N < 1 || M < 1 || K < tc::kBK || K % tc::kBK) return h->fail(VX_E_INVALID, "tensor-core GEMM shape %dx%dx%d", M, N, K);
   const int n_tiles = (N + BN - 1) / BN, m_tiles = (M + tc::kBM - 1) / tc::kBM;
   const int chunks = K / tc::kBK;
   const int tiles = n_tiles * m_tiles;
   int splits = 1;
-  if (tiles < h->num_sms) splits = std::min({chunks, max_splits, (h->num_sms + tiles - 1) / tiles});
-  while (splits > 1 && ((size_t)tiles * splits * BN * tc::kBM > h->tb_ws_floats || tiles > h->tb_max_tiles)) --splits;
+  if (tiles < h->num_sms) splits = std::max(1, std::min({chunks, max_splits, h->num_sms / tiles}));
+  if (M % 4 || ldy % 4) splits = 1;   // the split-K reduction writes float4 along m
+  while (splits > 1 && (size_t)tiles * splits * BN * tc::kBM > h->tb_ws_floats) --splits;
   const int cps = (chunks + splits - 1) / splits;
   splits = (chunks + cps - 1) / cps;
-  tc::Params p{y, ldy, h->tb_ws, h->tb_gemm_tickets, M, N, K, cps, accumulate};
+  tc::Params p{y, ldy, h->tb_ws, M, N, K, cps, accumulate};
   CK(launch(h, tc::k_gemm<BN>, dim3(n_tiles, m_tiles, splits), dim3(tc::kThreads), tc::Cfg<BN>::kSmem, w, xhi, xlo, p));
+  if (splits_out) {
+    *splits_out = splits > 1 ? splits : 0;   // the caller's row kernel sums the partials
+  } else if (splits > 1) {
+    tc::ReduceParams rp{h->tb_ws, y, ldy, M, N, splits, n_tiles, BN, accumulate};
+    const long long n4 = (long long)N * (M / 4);
+    CK(launch(h, tc::k_splitk_reduce, dim3((unsigned)std::min<long long>((n4 + 255) / 256, 4L * h->num_sms)), dim3(256),
+              0, rp));
+  }
+  return VX_OK;
+}
+
+// Per-row epilogue launch (k_tb_row): split-K sum + residual + RMSNorm -> hi/lo, or
+// split-K sum + RoPE + K/V append.
+int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float* y, long long ldy, int M,
+           const __half* norm_w, const tc::RopeKvParams* rope) {
+  tc::RowParams rp{};
+  rp.ws = h->tb_ws; rp.splits = splits; rp.n_tiles = n_tiles; rp.bn = bn; rp.y = y; rp.ldy = ldy; rp.M = M;
+  rp.mode = mode; rp.norm_w = norm_w; rp.eps = h->cfg.norm_eps; rp.hi = h->tb_hi; rp.lo = h->tb_lo;
+  if (rope) rp.rope = *rope;
+  if (M == 3072) CK(launch(h, tc::k_tb_row<3>, dim3(n), dim3(256), 0, rp));
+  else if (M == 6144) CK(launch(h, tc::k_tb_row<6>, dim3(n), dim3(256), 0, rp));
+  else if (M % 1024 == 0 && M / 1024 <= 8) {
+    switch (M / 1024) {
+      case 1: CK(launch(h, tc::k_tb_row<1>, dim3(n), dim3(256), 0, rp)); break;
+      case 2: CK(launch(h, tc::k_tb_row<2>, dim3(n), dim3(256), 0, rp)); break;
+      case 4: CK(launch(h, tc::k_tb_row<4>, dim3(n), dim3(256), 0, rp)); break;
+      default: return h->fail(VX_E_INVALID, "row width %d", M);
+    }
+  } else {
+    return h->fail(VX_E_INVALID, "row width %d", M);
+  }
+  return VX_OK;
+}
+
+// The L layers for a batch of n activation rows in tb_h (rows described by `tr`):
+// on entry tb_hi/tb_lo must hold RMSNorm(tb_h) * attention_norm of layer 0; on
+// exit tb_h holds the last layer's residual stream.  Per layer:
+//   GEMM [wq;wk;wv] -> row kernel (split-K sum, RoPE, q, K/V append) -> attention
+//   (writes the hi/lo operand of o_proj) -> GEMM wo -> row kernel (h +=, RMSNorm
+//   ffn_norm -> hi/lo) -> GEMM [w1;w3] -> SwiGLU -> GEMM w2 -> row kernel (h +=,
+//   RMSNorm of the next layer's attention_norm -> hi/lo).
+template <int BN>
+int tb_layers(vx_handle* h, int n, const tc::TokRows& tr, int slot0, int rows_consecutive, int nsb) {
+  const int D = h->D;
+  int rc, sp = 0;
+  const CUtensorMap* xh = BN == 64 ? h->tb_xhi64 : h->tb_xhi;
+  const CUtensorMap* xl = BN == 64 ? h->tb_xlo64 : h->tb_xlo;
+  const int n_tiles = (n + BN - 1) / BN;
+  gemv::KvGeom kg{h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV, kPage};
+  for (int l = 0; l < h->L; ++l) {
+    const LayerW& W = h->layers[l];
+    const vx_handle::TbLayerMaps& mp = h->tb_wmaps[l];
+    if ((rc = run_tc_gemm<BN>(h, mp.wqkv, xh[0], xl[0], h->tb_y, h->QKVD, h->QKVD, n, D, 0, 8, &sp))) return rc;
+    tc::RopeKvParams rp{nullptr, h->tb_q, h->QD, h->KVD, n, h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV,
+                        kPage, l, h->rope_freq, tr};
+    if ((rc = tb_row(h, n, tc::kRowQkv, sp, n_tiles, BN, h->tb_y, h->QKVD, h->QKVD, nullptr, &rp))) return rc;
+    attn::Params ap{};
+    ap.q = h->tb_q; ap.ldq = h->QD; ap.out = h->tb_att; ap.ldo = h->QD;
+    ap.part = h->tb_part; ap.tickets = h->tb_att_tickets;
+    ap.kv = kg; ap.layer = l; ap.pos = &h->slots[0].pos; ap.pos_stride = kPosStride; ap.slot0 = slot0;
+    ap.n_splits = nsb; ap.scale = 1.0f / sqrtf((float)h->HD); ap.rows_consecutive = rows_consecutive;
+    ap.out_hi = h->tb_hi; ap.out_lo = h->tb_lo;
+    CK(launch(h, attn::k_attn_decode, dim3(h->NKV, nsb, n), dim3(attn::kThreads), attn::kSmemBytes, h->kv_map, ap));
+    if ((rc = run_tc_gemm<BN>(h, mp.wo, xh[1], xl[1], h->tb_h, D, D, n, h->QD, 1, 8, &sp))) return rc;
+    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, n_tiles, BN, h->tb_h, D, D, W.ffn_norm, nullptr))) return rc;
+    if ((rc = run_tc_gemm<BN>(h, mp.w13, xh[0], xl[0], h->tb_y, 2LL * h->Fl, 2 * h->Fl, n, D, 0))) return rc;
+    const long long ng = (long long)n * h->Fl;
+    CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
+              dim3(256), 0, (const float*)h->tb_y, n, h->Fl, h->tb_hi, h->tb_lo));
+    if ((rc = run_tc_gemm<BN>(h, mp.w2, xh[2], xl[2], h->tb_h, D, D, n, h->Fl, 1, 8, &sp))) return rc;
+    const __half* next_norm = l + 1 < h->L ? h->layers[l + 1].attn_norm : nullptr;
+    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, n_tiles, BN, h->tb_h, D, D, next_norm, nullptr))) return rc;
+  }
   return VX_OK;
 }
 
@@ -646,49 +724,69 @@ int prefill_tb(vx_handle* h, int slot, int n) {
   const int D = h->D;
   int rc;
   tc::TokRows tr{&h->slots[0].pos, kPosStride, 0, slot};
-  gemv::KvGeom kg{h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV, kPage};
-  const float eps = h->cfg.norm_eps;
   int nc = 0;
   for (int c0 = 0; c0 < n; c0 += h->tb_cap) {
     nc = std::min(h->tb_cap, n - c0);
     tc::TbEmbedParams ep{h->tok_emb, h->V, h->prompt, h->voice, h->cfg.max_seq_len, h->cfg.max_voice_rows, D, h->tb_h, tr};
     CK(launch(h, tc::k_tb_embed, dim3(nc), dim3(256), 0, ep));
-    for (int l = 0; l < h->L; ++l) {
-      const LayerW& W = h->layers[l];
-      const vx_handle::TbLayerMaps& mp = h->tb_wmaps[l];
-      CK(launch(h, tc::k_tb_norm_split, dim3(nc), dim3(256), 0, (const float*)h->tb_h, (const __half*)W.attn_norm, D,
-                eps, h->tb_hi, h->tb_lo));
-      if ((rc = run_tc_gemm<128>(h, mp.wqkv, h->tb_xhi[0], h->tb_xlo[0], h->tb_y, h->QKVD, h->QKVD, nc, D, 0))) return rc;
-      tc::RopeKvParams rp{h->tb_y, h->tb_q, h->QD, h->KVD, nc, h->kv_pool, h->page_table, h->max_pages, h->L, h->NKV,
-                          kPage, l, h->rope_freq, tr};
-      CK(launch(h, tc::k_tb_rope_kv, dim3(nc), dim3(256), 0, rp));
-      attn::Params ap{};
-      ap.q = h->tb_q; ap.ldq = h->QD; ap.out = h->tb_att; ap.ldo = h->QD;
-      ap.part = h->tb_part; ap.tickets = h->tb_att_tickets;
-      ap.kv = kg; ap.layer = l; ap.pos = &h->slots[0].pos; ap.pos_stride = kPosStride; ap.slot0 = slot;
-      ap.n_splits = 1; ap.scale = 1.0f / sqrtf((float)h->HD); ap.rows_consecutive = 1;
-      CK(launch(h, attn::k_attn_decode, dim3(h->NKV, 1, nc), dim3(attn::kThreads), attn::kSmemBytes, h->kv_map, ap));
-      const long long na = (long long)nc * h->QD;
-      CK(launch(h, tc::k_tb_split, dim3((unsigned)std::min<long long>((na + 255) / 256, 4L * h->num_sms)), dim3(256), 0,
-                (const float*)h->tb_att, na, h->tb_hi, h->tb_lo));
-      if ((rc = run_tc_gemm<128>(h, mp.wo, h->tb_xhi[1], h->tb_xlo[1], h->tb_h, D, D, nc, h->QD, 1))) return rc;
-      CK(launch(h, tc::k_tb_norm_split, dim3(nc), dim3(256), 0, (const float*)h->tb_h, (const __half*)W.ffn_norm, D,
-                eps, h->tb_hi, h->tb_lo));
-      if ((rc = run_tc_gemm<128>(h, mp.w13, h->tb_xhi[0], h->tb_xlo[0], h->tb_y, 2LL * h->Fl, 2 * h->Fl, nc, D, 0)))
-        return rc;
-      const long long ng = (long long)nc * h->Fl;
-      CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
-                dim3(256), 0, (const float*)h->tb_y, nc, h->Fl, h->tb_hi, h->tb_lo));
-      if ((rc = run_tc_gemm<128>(h, mp.w2, h->tb_xhi[2], h->tb_xlo[2], h->tb_h, D, D, nc, h->Fl, 1))) return rc;
-    }
+    if ((rc = tb_row(h, nc, tc::kRowResidNorm, 0, 0, 128, h->tb_h, D, D, h->layers[0].attn_norm, nullptr))) return rc;
+    if ((rc = tb_layers<128>(h, nc, tr, slot, 1, 1))) return rc;
     CK(launch(h, tc::k_tb_advance, dim3(1), dim3(32), 0, &h->slots[slot].pos, nc));
   }
   // last position: final norm into `normed`, residual stream into `h`
   FinalNormParams fp{};
   fp.h = h->tb_h + (long long)(nc - 1) * D; fp.w = h->final_norm; fp.out = h->normed + (long long)slot * D; fp.D = D;
-  fp.eps = eps;
+  fp.eps = h->cfg.norm_eps;
   CK(launch(h, k_final_norm, dim3(1), dim3(256), 0, fp));
   CK(cudaMemcpyAsync(h->h + (long long)slot * D, fp.h, (size_t)D * 4, cudaMemcpyDeviceToDevice, h->stream));
+  return VX_OK;
+}
+
+// One backbone step of slots [slot0, slot0 + n) in lockstep, each at its own
+// position (the reference's per-frame backboneStep, src/engine.ts:814-1042, for n
+// utterances at once): embedding per slot, the token-batch layers (weights streamed
+// once per step for all slots), final norm per slot with the position / frame
+// advance and the normed-state record.
+template <int BN>
+int enqueue_decode_batch_bn(vx_handle* h, int slot0, int n) {
+  const int D = h->D;
+  int rc;
+  tc::TokRows tr{&h->slots[0].pos, kPosStride, 1, slot0};
+  EmbedParams ep{};
+  ep.tok = h->tok_emb; ep.vocab = h->V; ep.audio = h->audio_emb; ep.audio_rows = h->AV;
+  ep.slots = h->slots; ep.rows = h->rows_in; ep.prompt = h->prompt; ep.voice = h->voice;
+  ep.max_seq = h->cfg.max_seq_len; ep.max_voice = h->cfg.max_voice_rows; ep.code_ring = h->code_ring;
+  ep.h = h->tb_h; ep.D = D; ep.slot0 = slot0;
+  CK(launch(h, k_embed, dim3(n), dim3(256), 0, ep));
+  if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 0, BN, h->tb_h, D, D, h->layers[0].attn_norm, nullptr))) return rc;
+  // attention partials hold tb_cap x n_kv x 1 split: n rows x nsb splits must fit
+  const int nsb = std::max(1, std::min(h->tb_attn_splits, h->tb_cap / n));
+  if ((rc = tb_layers<BN>(h, n, tr, slot0, 0, nsb))) return rc;
+  FinalNormParams fp{};
+  fp.h = h->tb_h; fp.w = h->final_norm; fp.out = h->normed + (long long)slot0 * D; fp.D = D; fp.eps = h->cfg.norm_eps;
+  fp.slots = h->slots; fp.slot0 = slot0; fp.inc_pos = 1; fp.inc_frame = 1; fp.normed_ring = h->normed_ring;
+  CK(launch(h, k_final_norm, dim3(n), dim3(256), 0, fp));
+  return VX_OK;
+}
+
+int run_decode_batch(vx_handle* h, int slot0, int n) {
+  vx_handle::G& g = h->g_batch[((long long)slot0 << 20) | n];
+  if (!g.exec) {
+    cudaGraph_t graph;
+    const long long before = h->launches;
+    CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = n <= 64 ? enqueue_decode_batch_bn<64>(h, slot0, n) : enqueue_decode_batch_bn<128>(h, slot0, n);
+    cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+    if (rc) { if (ce == cudaSuccess) cudaGraphDestroy(graph); return rc; }
+    if (ce != cudaSuccess) return h->fail(VX_E_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+    cudaError_t ie = cudaGraphInstantiate(&g.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return h->fail(VX_E_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
+    g.kernels = h->launches - before;
+    h->launches = before;
+  }
+  CK(cudaGraphLaunch(g.exec, h->stream));
+  h->launches += g.kernels;
   return VX_OK;
 }
 
@@ -700,12 +798,11 @@ int setup_tb(vx_handle* h) {
   const long long kmax = std::max<long long>({D, (long long)h->QD, (long long)h->Fl});
   const long long ymax = std::max<long long>(h->QKVD, 2LL * h->Fl);
   h->tb_ws_floats = (size_t)8 << 20;
-  h->tb_max_tiles = 4096;
   size_t bytes = 0;
   auto add = [&](size_t b) { bytes += (b + 255) & ~size_t(255); };
   add(cap * D * 4); add(cap * ymax * 4); add(cap * h->QD * 4); add(cap * h->QD * 4);
   add(cap * h->NKV * attn::kGqa * attn::kPartStride * 4); add(h->tb_ws_floats * 4);
-  add(cap * h->NKV * 4); add((size_t)h->tb_max_tiles * 4); add(cap * kmax * 2); add(cap * kmax * 2);
+  add(cap * h->NKV * 4); add(cap * kmax * 2); add(cap * kmax * 2);
   if (cudaMalloc(&h->tb_buf, bytes) != cudaSuccess) return h->fail(VX_E_NOMEM, "token-batch buffers (%.1f MB)", bytes / 1e6);
   CK(cudaMemset(h->tb_buf, 0, bytes));
   uint8_t* cur = (uint8_t*)h->tb_buf;
@@ -716,7 +813,6 @@ int setup_tb(vx_handle* h) {
   h->tb_part = (float*)carve(cur, cap * h->NKV * attn::kGqa * attn::kPartStride * 4);
   h->tb_ws = (float*)carve(cur, h->tb_ws_floats * 4);
   h->tb_att_tickets = (int*)carve(cur, cap * h->NKV * 4);
-  h->tb_gemm_tickets = (int*)carve(cur, (size_t)h->tb_max_tiles * 4);
   h->tb_hi = (__half*)carve(cur, cap * kmax * 2);
   h->tb_lo = (__half*)carve(cur, cap * kmax * 2);
   int rc;
@@ -724,6 +820,8 @@ int setup_tb(vx_handle* h) {
   for (int i = 0; i < 3; ++i) {
     if ((rc = encode_f16_2d(h, &h->tb_xhi[i], h->tb_hi, ks[i], cap, ks[i] * 2, tc::kBK, 128))) return rc;
     if ((rc = encode_f16_2d(h, &h->tb_xlo[i], h->tb_lo, ks[i], cap, ks[i] * 2, tc::kBK, 128))) return rc;
+    if ((rc = encode_f16_2d(h, &h->tb_xhi64[i], h->tb_hi, ks[i], cap, ks[i] * 2, tc::kBK, 64))) return rc;
+    if ((rc = encode_f16_2d(h, &h->tb_xlo64[i], h->tb_lo, ks[i], cap, ks[i] * 2, tc::kBK, 64))) return rc;
   }
   h->tb_wmaps.resize(h->L);
   for (int l = 0; l < h->L; ++l) {
@@ -1012,6 +1110,9 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   {
     const char* e = getenv("VX_NO_BATCHED_PREFILL");
     h->use_tb = h->tp == 1 && !(e && e[0] == '1');
+    if (const char* as = getenv("VX_BATCH_ATTN_SPLITS")) h->tb_attn_splits = std::max(1, std::min(8, atoi(as)));
+    const char* tw = getenv("VX_PREFILL_TOKENWISE");
+    h->prefill_tokenwise = tw && tw[0] == '1';
     if (h->use_tb && (rc = setup_tb(h))) { *out = h; return rc; }
   }
   *out = h;
@@ -1025,6 +1126,8 @@ void vx_destroy(vx_handle* h) {
   for (auto* tab : {&h->g_step, &h->g_fm, &h->g_frame_fm, &h->g_frame_bb})
     for (auto& g : *tab)
       if (g.exec) cudaGraphExecDestroy(g.exec);
+  for (auto& kv : h->g_batch)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   if (h->comm && g_nccl.commDestroy) g_nccl.commDestroy(h->comm);
   if (h->arena) cudaFree(h->arena);
   if (h->d_layers) cudaFree(h->d_layers);
@@ -1240,7 +1343,7 @@ int vx_prefill(vx_handle* h, int32_t slot, const int32_t* tokens, int32_t n, int
   u.set_mode = 1; u.mode = kEmbPrompt; u.token = 0;
   u.set_prompt_len = 1; u.prompt_len = p0 + n;
   if ((rc = slot_update(h, slot, u))) return rc;
-  if (h->use_tb) {
+  if (h->use_tb && !h->prefill_tokenwise) {
     if ((rc = prefill_tb(h, slot, n))) return rc;
   } else if (h->use_mk) {
     if ((rc = launch_steps(h, slot, n, kEmbPrompt, 0, kEmbPrompt, false, false))) return rc;
@@ -1411,6 +1514,43 @@ int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm) {
     }
   }
   h->frame_host[slot] = f0 + n_frames;
+  return VX_OK;
+}
+
+int vx_decode_batch(vx_handle* h, int32_t slot0, int32_t n_slots, int32_t n_frames) {
+  if (!h) return VX_E_INVALID;
+  int rc;
+  if (n_slots < 1 || slot0 < 0 || slot0 + n_slots > h->B)
+    return h->fail(VX_E_RANGE, "slots [%d, %d) outside [0, %d)", slot0, slot0 + n_slots, h->B);
+  if (n_frames < 0) return h->fail(VX_E_INVALID, "n_frames");
+  if ((rc = check_slot(h, slot0))) return rc;
+  if (!h->use_tb) return h->fail(VX_E_STATE, "batched decode needs the token-batch path (tp_size 1)");
+  if (n_slots > h->tb_cap) return h->fail(VX_E_RANGE, "%d slots exceed the batch capacity %d", n_slots, h->tb_cap);
+  if (n_frames == 0) return VX_OK;
+  for (int s = slot0; s < slot0 + n_slots; ++s) {
+    if ((rc = need_positions(h, s, n_frames))) return rc;
+    if (h->frame_host[s] + n_frames > h->cfg.max_frames)
+      return h->fail(VX_E_RANGE, "slot %d: frames %d + %d exceed the code ring (%d)", s, h->frame_host[s], n_frames,
+                     h->cfg.max_frames);
+  }
+  CK(cudaSetDevice(h->dev));
+  // frame 0 of a slot is the AUDIO kick; later frames are fed the synthetic codes
+  bool any_kick = false;
+  for (int s = slot0; s < slot0 + n_slots; ++s) {
+    const bool kick = h->frame_host[s] == 0;
+    any_kick |= kick;
+    if ((rc = set_slot_fields(h, s, kick ? kEmbToken : kEmbSynthCodes, kick ? kAudioKick : 0))) return rc;
+  }
+  for (int f = 0; f < n_frames; ++f) {
+    if ((rc = run_decode_batch(h, slot0, n_slots))) return rc;
+    if (f == 0 && any_kick)
+      for (int s = slot0; s < slot0 + n_slots; ++s)
+        if ((rc = set_slot_fields(h, s, kEmbSynthCodes, 0))) return rc;
+  }
+  for (int s = slot0; s < slot0 + n_slots; ++s) {
+    h->pos_host[s] += n_frames;
+    h->frame_host[s] += n_frames;
+  }
   return VX_OK;
 }
 

@@ -91,6 +91,7 @@ def load_library():
         "vx_fm_step": (ctypes.c_int, [H, ctypes.c_int32, _f32p, _f32p, _u32p, _u32p, _f32p]),
         "vx_debug_layers": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p]),
         "vx_decode": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+        "vx_decode_batch": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
         "vx_set_streams": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int32]),
         "vx_read_codes": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _u32p]),
         "vx_read_normed": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f32p]),
@@ -355,6 +356,12 @@ class VoxtralEngine:
         """Enqueue n_frames device-resident frames (no host round trip); asynchronous."""
         self._require_ready()
         self._check(load_library().vx_decode(self._h, slot, n_frames, int(with_fm)))
+
+    def decode_batch(self, n_frames: int, n_slots: int, slot0: int = 0):
+        """Backbone-only decode of n_frames frames for slots [slot0, slot0+n_slots) in lockstep
+        (tensor-core GEMMs over the slots); asynchronous."""
+        self._require_ready()
+        self._check(load_library().vx_decode_batch(self._h, slot0, n_slots, n_frames))
 
     def read_codes(self, frame0: int, n: int, slot: int = 0) -> np.ndarray:
         out = np.empty((n, 37), np.uint32)
