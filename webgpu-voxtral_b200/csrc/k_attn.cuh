@@ -242,9 +242,22 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const __grid_constant_
         O += ww[2 + d] * f;
       }
     }
+    if (p.n_splits == 1) {
+      // one split: this CTA holds the whole softmax, write the output directly
+      const float v = L > 0.f ? O / L : 0.f;
+      const long long oi = (long long)row * p.ldo + (long long)(kvh * kGqa + h) * kHd + d;
+      p.out[oi] = v;
+      if (p.out_hi) {
+        const __half hh = __float2half_rn(v);
+        p.out_hi[oi] = hh;
+        p.out_lo[oi] = __float2half_rn(v - __half2float(hh));
+      }
+      continue;
+    }
     part[h * kPartStride + 2 + d] = O;
     if (d == 0) { part[h * kPartStride] = M; part[h * kPartStride + 1] = L; }
   }
+  if (p.n_splits == 1) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {

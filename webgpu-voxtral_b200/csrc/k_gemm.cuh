@@ -275,27 +275,6 @@ __device__ __forceinline__ void split_store(__half* hi, __half* lo, long long i,
   lo[i] = __float2half_rn(x - __half2float(h));
 }
 
-// Row-wise RMSNorm (src/shaders.ts:137-183: x * (1/sqrt(mean(x^2) + eps)) * w) of
-// X[N, D] into the hi/lo operand pair.  One CTA (256 threads) per row.
-__global__ void __launch_bounds__(256) k_tb_norm_split(const float* __restrict__ x, const __half* __restrict__ w,
-                                                        int D, float eps, __half* hi, __half* lo) {
-  griddep_launch();
-  griddep_wait();
-  __shared__ float sh[8];
-  const float* xr = x + (long long)blockIdx.x * D;
-  float s = 0.f;
-  for (int i = threadIdx.x; i < D; i += 256) s += xr[i] * xr[i];
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += sh[i];
-  const float rms = 1.0f / sqrtf(tot / (float)D + eps);
-  const long long base = (long long)blockIdx.x * D;
-  for (int i = threadIdx.x; i < D; i += 256) split_store(hi, lo, base + i, xr[i] * rms * __half2float(w[i]));
-}
-
 // X[N, K] f32 -> hi/lo pair (attention output feeding o_proj).
 __global__ void k_tb_split(const float* __restrict__ x, long long n, __half* hi, __half* lo) {
   griddep_launch();
@@ -318,9 +297,9 @@ __global__ void k_tb_swiglu_split(const float* __restrict__ y13, int N, int F, _
 }
 
 // RoPE (src/shaders.ts:224-256, interleaved pairs, angle = pos * freq) on the q
-// and k parts of QKV[N, q_dim + 2 kv_dim], q -> Q[N, q_dim] (f32), K/V appended to
-// the paged f16 cache at each row's position (src/shaders.ts:452-473).  The
-// rotation arithmetic is that of the decode kernels' QKV epilogue.
+// and k parts of a QKV row [q_dim + 2 kv_dim], q -> Q[N, q_dim] (f32), K/V appended
+// to the paged f16 cache at the row's position (src/shaders.ts:452-473), with the
+// rotation arithmetic of the decode kernels' QKV epilogue (k_tb_row, kRowQkv).
 struct RopeKvParams {
   const float* qkv;
   float* q;
@@ -331,51 +310,13 @@ struct RopeKvParams {
   const float* rope_freq;
   TokRows rows;
 };
-__global__ void __launch_bounds__(256) k_tb_rope_kv(const __grid_constant__ RopeKvParams p) {
-  griddep_launch();
-  griddep_wait();
-  const int r = blockIdx.x;
-  const int slot = tok_slot(p.rows, r), pos = tok_pos(p.rows, r);
-  const int width = p.q_dim + 2 * p.kv_dim;
-  const float* src = p.qkv + (long long)r * width;
-  const int lp = pos / p.page_size;
-  const bool page_ok = pos >= 0 && lp < p.max_pages;
-  if (!page_ok && threadIdx.x == 0) set_error(kDevBadIndex);
-  const int page = page_ok ? p.page_table[(long long)slot * p.max_pages + lp] : 0;
-  for (int i = threadIdx.x; i < width; i += 256) {
-    const float val = src[i];
-    float out = val;
-    if (i < p.q_dim + p.kv_dim) {
-      const float other = src[i ^ 1];
-      const int pair = (i & 127) >> 1;
-      const float ang = (float)pos * p.rope_freq[pair];
-      float sn, cs;
-      sincosf(ang, &sn, &cs);
-      const bool even = (i & 1) == 0;
-      const float x0 = even ? val : other, x1 = even ? other : val;
-      out = even ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-    }
-    if (i < p.q_dim) {
-      p.q[(long long)r * p.q_dim + i] = out;
-    } else if (page_ok) {
-      const int kvr = i - p.q_dim;
-      const int kv = kvr >= p.kv_dim ? 1 : 0;
-      const int rr = kvr - kv * p.kv_dim;
-      const int head = rr >> 7, d = rr & 127;
-      const long long prow =
-          ((((long long)page * p.n_layers + p.layer) * 2 + kv) * p.n_kv + head) * p.page_size + pos % p.page_size;
-      p.pool[prow * 128 + d] = __float2half_rn(out);
-    }
-  }
-}
-
-// Per-row epilogue of a token-batch GEMM, one CTA (256 threads) per activation
-// row n: sums the split-K partials of the row in split order (splits == 0: the
+// Per-row epilogue of a token-batch GEMM, one CTA per activation row n: sums the split-K partials of the row in split order (splits == 0: the
 // GEMM wrote its result to Y itself) and then
-//   kRowResidNorm: h[n] += partials; x' = RMSNorm(h[n]) * w -> hi/lo operand pair
-//                  of the next GEMM (norm_w null: no operand output);
+//   kRowResidNorm: h[n] += partials; x' = RMSNorm(h[n]) * w (src/shaders.ts:137-183:
+//                  x * (1/sqrt(mean(x^2) + eps)) * w) -> hi/lo operand pair of the
+//                  next GEMM (norm_w null: no operand output);
 //   kRowQkv:       RoPE on the q / k parts, q -> Q[n], K/V appended to the paged
-//                  cache at the row's position (the math of k_tb_rope_kv).
+//                  cache at the row's position.
 enum RowMode { kRowResidNorm = 0, kRowQkv = 1 };
 struct RowParams {
   const float* ws;
@@ -389,26 +330,32 @@ struct RowParams {
   __half *hi, *lo;           // [N][M]
   RopeKvParams rope;         // kRowQkv (rope.qkv unused)
 };
-template <int V4>   // float4 groups per thread: M = 4 * 256 * V4
-__global__ void __launch_bounds__(256) k_tb_row(const __grid_constant__ RowParams p) {
+// Launched with M / 12 threads per row: each thread owns 3 float4 groups and issues
+// the loads of every split at once (up to kMaxRowSplits in flight).
+constexpr int kMaxRowSplits = 8;
+__global__ void __launch_bounds__(512) k_tb_row(const __grid_constant__ RowParams p) {
   griddep_launch();
   griddep_wait();
-  __shared__ float sh[8];
+  __shared__ float sh[16];
   const int n = blockIdx.x;
-  float4 v[V4];
+  const int nt = blockDim.x;
+  float4 v[3];
 #pragma unroll
-  for (int u = 0; u < V4; ++u) {
-    const int m = (threadIdx.x + 256 * u) * 4;
+  for (int u = 0; u < 3; ++u) {
+    const int m = (threadIdx.x + nt * u) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.splits == 0) {
       acc = *reinterpret_cast<const float4*>(p.y + (long long)n * p.ldy + m);
     } else {
       const int tile = (m / kBM) * p.n_tiles + n / p.bn;
       const float* src = p.ws + ((long long)tile * p.splits * p.bn + n % p.bn) * kBM + m % kBM;
-      for (int s = 0; s < p.splits; ++s) {
-        const float4 w = __ldcg(reinterpret_cast<const float4*>(src + (long long)s * p.bn * kBM));
-        acc.x += w.x; acc.y += w.y; acc.z += w.z; acc.w += w.w;
-      }
+      float4 w[kMaxRowSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxRowSplits; ++s)
+        if (s < p.splits) w[s] = __ldcg(reinterpret_cast<const float4*>(src + (long long)s * p.bn * kBM));
+#pragma unroll
+      for (int s = 0; s < kMaxRowSplits; ++s)
+        if (s < p.splits) { acc.x += w[s].x; acc.y += w[s].y; acc.z += w[s].z; acc.w += w[s].w; }
       if (p.mode == kRowResidNorm) {
         const float4 h = *reinterpret_cast<const float4*>(p.y + (long long)n * p.ldy + m);
         acc = make_float4(h.x + acc.x, h.y + acc.y, h.z + acc.z, h.w + acc.w);
@@ -421,17 +368,16 @@ __global__ void __launch_bounds__(256) k_tb_row(const __grid_constant__ RowParam
     if (!p.norm_w) return;
     float ss = 0.f;
 #pragma unroll
-    for (int u = 0; u < V4; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    for (int u = 0; u < 3; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) tot += sh[i];
+    for (int i = 0; i < (nt >> 5); ++i) tot += sh[i];
     const float rms = 1.0f / sqrtf(tot / (float)p.M + p.eps);
 #pragma unroll
-    for (int u = 0; u < V4; ++u) {
-      const int m = (threadIdx.x + 256 * u) * 4;
+    for (int u = 0; u < 3; ++u) {
+      const int m = (threadIdx.x + nt * u) * 4;
       const __half2* w2 = reinterpret_cast<const __half2*>(p.norm_w + m);
       const float2 wa = __half22float2(w2[0]), wb = __half22float2(w2[1]);
       const long long o = (long long)n * p.M + m;
@@ -450,8 +396,8 @@ __global__ void __launch_bounds__(256) k_tb_row(const __grid_constant__ RowParam
   if (!page_ok && threadIdx.x == 0) set_error(kDevBadIndex);
   const int page = page_ok ? r.page_table[(long long)slot * r.max_pages + lp] : 0;
 #pragma unroll
-  for (int u = 0; u < V4; ++u) {
-    const int m = (threadIdx.x + 256 * u) * 4;
+  for (int u = 0; u < 3; ++u) {
+    const int m = (threadIdx.x + nt * u) * 4;
     float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
     if (m < r.q_dim + r.kv_dim) {
 #pragma unroll

@@ -657,18 +657,9 @@ int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float
   rp.ws = h->tb_ws; rp.splits = splits; rp.n_tiles = n_tiles; rp.bn = bn; rp.y = y; rp.ldy = ldy; rp.M = M;
   rp.mode = mode; rp.norm_w = norm_w; rp.eps = h->cfg.norm_eps; rp.hi = h->tb_hi; rp.lo = h->tb_lo;
   if (rope) rp.rope = *rope;
-  if (M == 3072) CK(launch(h, tc::k_tb_row<3>, dim3(n), dim3(256), 0, rp));
-  else if (M == 6144) CK(launch(h, tc::k_tb_row<6>, dim3(n), dim3(256), 0, rp));
-  else if (M % 1024 == 0 && M / 1024 <= 8) {
-    switch (M / 1024) {
-      case 1: CK(launch(h, tc::k_tb_row<1>, dim3(n), dim3(256), 0, rp)); break;
-      case 2: CK(launch(h, tc::k_tb_row<2>, dim3(n), dim3(256), 0, rp)); break;
-      case 4: CK(launch(h, tc::k_tb_row<4>, dim3(n), dim3(256), 0, rp)); break;
-      default: return h->fail(VX_E_INVALID, "row width %d", M);
-    }
-  } else {
-    return h->fail(VX_E_INVALID, "row width %d", M);
-  }
+  if (M % 12 || M / 12 > 512 || (M / 12) % 32) return h->fail(VX_E_INVALID, "row width %d", M);
+  if (splits > tc::kMaxRowSplits) return h->fail(VX_E_INVALID, "%d split-K partials per row", splits);
+  CK(launch(h, tc::k_tb_row, dim3(n), dim3(M / 12), 0, rp));
   return VX_OK;
 }
 
