@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--mode", default="dp", choices=["dp", "tp"],
                     help="N > 1: dp = one utterance per GPU (weak scaling); tp = one utterance over N GPUs")
     ap.add_argument("--c3-frames", type=int, default=40, help="frames of the backbone+FM (C3) sample; 0 = skip")
+    ap.add_argument("--c4-slots", type=int, default=64, help="utterances decoded in lockstep per GPU (C4)")
+    ap.add_argument("--c4-frames", type=int, default=1500, help="frames of the batched (C4) run; 0 = skip")
     return ap.parse_args()
 
 
@@ -187,6 +189,56 @@ def run_reference(args):
     return 0
 
 
+def run_c4(args, vx, synth, local, stream):
+    """C4: S utterances per GPU (prompt 256 text ids + 100 voice rows each),
+    decoded in lockstep for F frames with vx_decode_batch (tensor-core GEMMs over the
+    slots, paged f16 KV).  Times the whole F-frame run with CUDA events (inputs resident)."""
+    import torch
+    S, F4 = args.c4_slots, args.c4_frames
+    eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": args.layers}}, "maxSeqLen": 2048,
+                            "maxFrames": F4 + 8, "enableFM": False, "device": local, "maxSlots": S})
+    eng.init()
+    eng.loadRandomWeights(0)
+    eng.set_stream(stream.cuda_stream)
+    p0 = None
+    for u in range(S):
+        toks, a0, na = synth.prompt(1000 + u, 256, 100)
+        eng.reset(slot=u)
+        eng.set_streams(3, 4, 1000 + u, slot=u)
+        eng.prefill(toks, a0, na, synth.voice_rows(1000 + u, 100), slot=u)
+        p0 = len(toks)
+    eng.synchronize()
+    for u in range(S):
+        eng.checkpoint(slot=u)
+    eng.decode_batch(4, S)                    # warm-up: graph capture
+    for u in range(S):
+        eng.rewind(slot=u)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = eng.launch_count()
+    e0.record(stream)
+    eng.decode_batch(F4, S)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = eng.launch_count() - l0
+    eng.destroy()
+    step_ms = ms / F4
+    avg_pos = p0 + (F4 - 1) / 2
+    step_bytes = args.layers * BYTES_PER_LAYER + 6144 + S * (37 * 3072 * 2 + (avg_pos + 1) * KV_BYTES_PER_POS * args.layers / 26)
+    flops = 2.0 * S * args.layers * (BYTES_PER_LAYER / 2)
+    peak, kind = measured_peaks()
+    return {"workload": f"C4: {S} utterances per GPU in lockstep (prompt 256 text ids + 100 voice rows = {p0} positions "
+                        f"each), {F4} frames, paged f16 KV, maxSeqLen 2048; weights streamed once per step for all slots",
+            "frames_per_s": S * F4 / (ms / 1e3), "ms_per_step": step_ms, "slots": S, "frames": F4,
+            "avg_position": avg_pos, "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
+                         "achieved": step_bytes / (step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak_kind": kind},
+            "tensor": {"gemm_tflops_per_step": flops / (step_ms / 1e3) / 1e12,
+                       "note": "2 flops per weight per slot; the tensor cores run twice that (activations as f16 hi + lo)"}}
+
+
 def run_b200(args):
     import torch
 
@@ -310,6 +362,11 @@ def run_b200(args):
               "fm_bytes_per_frame": 4961851392,
               "frame_gbs": (frame_bytes + 4961851392) / (c3_ms / 1e3) / 1e9}
 
+    # ------------------------------------------------------------------ C4: batched lockstep decode
+    c4 = None
+    if args.c4_frames > 0 and tp == 1:
+        c4 = run_c4(args, vx, synth, local, stream)
+
     # ------------------------------------------------------------------ end to end through the C ABI
     e2e_vals, h2d, d2h = [], 0, 0
     for i in range(2):
@@ -358,6 +415,7 @@ def run_b200(args):
                              "full_ms_per_frame": prof["step_ms"]}},
             "c3_backbone_plus_fm": c3,
             "prefill": prefill,
+            "c4_batched": c4,
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
