@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--c3-frames", type=int, default=40, help="frames of the backbone+FM (C3) sample; 0 = skip")
     ap.add_argument("--c4-slots", type=int, default=64, help="utterances decoded in lockstep per GPU (C4)")
     ap.add_argument("--c4-frames", type=int, default=1500, help="frames of the batched (C4) run; 0 = skip")
+    ap.add_argument("--c5-slots", type=int, default=16, help="utterances of the long-context (C5) run")
+    ap.add_argument("--c5-context", type=int, default=32768, help="synthetic K/V positions per utterance (C5)")
+    ap.add_argument("--c5-frames", type=int, default=256, help="frames of the long-context (C5) run; 0 = skip")
     return ap.parse_args()
 
 
@@ -239,6 +242,48 @@ def run_c4(args, vx, synth, local, stream):
                        "note": "2 flops per weight per slot; the tensor cores run twice that (activations as f16 hi + lo)"}}
 
 
+def run_c5(args, vx, local, stream):
+    """C5 on one GPU: S utterances whose K/V cache holds P synthetic
+    positions (f16 N(0,1), vx_fill_kv), decoded F frames in lockstep (vx_decode_batch,
+    split-KV attention).  The KV stream dominates: S * P * 106,496 bytes per step."""
+    import torch
+    S, P, F5 = args.c5_slots, args.c5_context, args.c5_frames
+    eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": args.layers}}, "maxSeqLen": P + F5 + 8,
+                            "maxFrames": F5 + 8, "enableFM": False, "device": local, "maxSlots": S,
+                            "maxVoiceRows": 1})
+    eng.init()
+    eng.loadRandomWeights(0)
+    eng.set_stream(stream.cuda_stream)
+    for u in range(S):
+        eng.reset(slot=u)
+        eng.set_streams(3, 4, 2000 + u, slot=u)
+        eng.fill_kv(P, seed=5000 + u, slot=u)
+        eng.checkpoint(slot=u)
+    eng.decode_batch(2, S)                    # warm-up: graph capture
+    for u in range(S):
+        eng.rewind(slot=u)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    eng.decode_batch(F5, S)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    eng.destroy()
+    step_ms = ms / F5
+    avg_pos = P + (F5 - 1) / 2
+    kv = S * (avg_pos + 1) * KV_BYTES_PER_POS * args.layers / 26
+    step_bytes = args.layers * BYTES_PER_LAYER + 6144 + S * 37 * 3072 * 2 + kv
+    peak, kind = measured_peaks()
+    return {"workload": f"C5 on one GPU: {S} utterances with {P} synthetic f16 K/V positions each (vx_fill_kv), "
+                        f"{F5} frames in lockstep, split-KV flash-decode over the paged cache",
+            "frames_per_s": S * F5 / (ms / 1e3), "ms_per_step": step_ms, "slots": S, "frames": F5,
+            "avg_position": avg_pos, "kv_bytes_per_step": kv,
+            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
+                         "achieved": step_bytes / (step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak_kind": kind}}
+
+
 def run_b200(args):
     import torch
 
@@ -367,6 +412,10 @@ def run_b200(args):
     if args.c4_frames > 0 and tp == 1:
         c4 = run_c4(args, vx, synth, local, stream)
 
+    c5 = None
+    if args.c5_frames > 0 and tp == 1:
+        c5 = run_c5(args, vx, local, stream)
+
     # ------------------------------------------------------------------ end to end through the C ABI
     e2e_vals, h2d, d2h = [], 0, 0
     for i in range(2):
@@ -416,6 +465,7 @@ def run_b200(args):
             "c3_backbone_plus_fm": c3,
             "prefill": prefill,
             "c4_batched": c4,
+            "c5_long_context": c5,
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),

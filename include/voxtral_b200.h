@@ -155,6 +155,15 @@ int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm);
  * step for all slots.  Needs tp_size 1; n_slots <= 512. */
 int vx_decode_batch(vx_handle* h, int32_t slot0, int32_t n_slots, int32_t n_frames);
 
+/* Synthetic long context (long-context benchmark configuration): K/V of positions
+ * [0, n_positions) of every layer of the slot = f16(N(0,1)) from the counter-based
+ * generator (stream (seed, 2*layer + kv), counter pos*1024 + head*128 + d), then the
+ * slot's position = n_positions and frame = 0, as if a prompt of that length had been
+ * prefilled.  No counterpart in the reference (its prefill is the only way to fill
+ * the cache, src/engine.ts:2457-2472); the CPU oracle's orc_fill_kv draws the same
+ * values in f32. */
+int vx_fill_kv(vx_handle* h, int32_t slot, int32_t n_positions, uint64_t seed);
+
 /* Seeds of the slot's synthetic streams (FM noise, backbone-only feedback codes);
  * `utt` selects the utterance stream of vx_rng.h. */
 int vx_set_streams(vx_handle* h, int32_t slot, uint64_t noise_seed, uint64_t codes_seed, int32_t utt);

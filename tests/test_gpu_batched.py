@@ -148,3 +148,36 @@ def test_batched_decode_matches_oracle(vx, synth):
             assert max_abs_rel(got[f], ref["normed"][f]) < TOL, f
     finally:
         e.destroy()
+
+
+def test_long_context_fill_and_batched_decode_matches_oracle(vx, synth):
+    """Long-context form (C5): a synthetic 3000-position K/V context per slot
+    (vx_fill_kv), then batched decode with split-KV attention, against the oracle
+    filled with the same generator (f32 there, f16 in the engine's cache)."""
+    n, frames, npos = 3, 4, 3000
+    e = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 3072, "maxFrames": 16,
+                          "enableFM": False, "maxSlots": n})
+    e.init()
+    e.loadRandomWeights(0)
+    try:
+        for s in range(n):
+            e.reset(slot=s)
+            e.set_streams(noise_seed=3, codes_seed=4, utt=40 + s, slot=s)
+            e.fill_kv(npos, seed=100 + s, slot=s)
+        assert e.position(1) == npos
+        e.decode_batch(frames, n)
+        s = 1
+        o = oracle.Oracle(n_layers=2, max_seq=3072, with_fm=False)
+        o.fill_kv(npos, seed=100 + s)
+        codes = synth.feedback_codes(40 + s, 0, frames)
+        ref = [o.backbone_step(24)["normed"]]
+        for f in range(1, frames):
+            emb = o.multi_codebook_embed(int(codes[f - 1][0]), codes[f - 1][1:])
+            ref.append(o.backbone_step(embed=emb)["normed"])
+        o.close()
+        got = e.read_normed(0, frames, slot=s)
+        assert np.array_equal(e.read_codes(0, frames - 1, slot=s), codes[: frames - 1])
+        for f in range(frames):
+            assert max_abs_rel(got[f], ref[f]) < TOL, f
+    finally:
+        e.destroy()

@@ -82,6 +82,36 @@ __global__ void k_fill_normal_f16_kv(__half* pool, long long rows, uint64_t key)
     pool[i] = __float2half_rn(vx_normal(key, (uint64_t)i));
 }
 
+// Synthetic context for long-context runs: K/V of positions [0, npos) of every
+// layer of one slot = f16(N(0,1)) from stream (seed, 2*layer + kv) at counter
+// pos * kv_width + head * 128 + d (kv_width = all KV heads; head0 = first KV head
+// held by this tensor-parallel rank).  The CPU oracle's fill (orc_fill_kv) draws the
+// same values in f32.
+struct FillKvParams {
+  __half* pool;
+  const int32_t* page_table;
+  int slot, max_pages, n_layers, n_kv_local, head0, kv_width, npos, page_size;
+  uint64_t seed;
+};
+__global__ void k_fill_kv_slot(const __grid_constant__ FillKvParams p) {
+  const long long total = (long long)p.n_layers * 2 * p.npos * p.n_kv_local * 128;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i & 127);
+    long long t = i >> 7;
+    const int hl = (int)(t % p.n_kv_local);
+    t /= p.n_kv_local;
+    const int pos = (int)(t % p.npos);
+    t /= p.npos;
+    const int kv = (int)(t & 1), layer = (int)(t >> 1);
+    const uint64_t key = vx_stream_key(p.seed, 2ull * layer + kv);
+    const float v = vx_normal(key, (uint64_t)pos * p.kv_width + (uint64_t)(p.head0 + hl) * 128 + d);
+    const int page = p.page_table[(long long)p.slot * p.max_pages + pos / p.page_size];
+    const long long row =
+        ((((long long)page * p.n_layers + layer) * 2 + kv) * p.n_kv_local + hl) * p.page_size + pos % p.page_size;
+    p.pool[row * 128 + d] = __float2half_rn(v);
+  }
+}
+
 // ------------------------------------------------------------------ embedding
 struct EmbedParams {
   const __half* tok;   int vocab;

@@ -169,7 +169,7 @@ struct vx_handle {
   int* tb_att_tickets = nullptr;
   __half *tb_hi = nullptr, *tb_lo = nullptr;
   size_t tb_ws_floats = 0;
-  int tb_attn_splits = 2;              // attention splits per (slot, KV head) in batched decode (VX_BATCH_ATTN_SPLITS)
+  int tb_attn_splits = 0;              // attention splits per (slot, KV head) in batched decode; 0: by context length
 
   // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
   int parts = 7;          // kPartMisc | kPartGemv | kPartAttn
@@ -739,7 +739,7 @@ int prefill_tb(vx_handle* h, int slot, int n) {
 // once per step for all slots), final norm per slot with the position / frame
 // advance and the normed-state record.
 template <int BN>
-int enqueue_decode_batch_bn(vx_handle* h, int slot0, int n) {
+int enqueue_decode_batch_bn(vx_handle* h, int slot0, int n, int nsb) {
   const int D = h->D;
   int rc;
   tc::TokRows tr{&h->slots[0].pos, kPosStride, 1, slot0};
@@ -750,8 +750,6 @@ int enqueue_decode_batch_bn(vx_handle* h, int slot0, int n) {
   ep.h = h->tb_h; ep.D = D; ep.slot0 = slot0;
   CK(launch(h, k_embed, dim3(n), dim3(256), 0, ep));
   if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 0, BN, h->tb_h, D, D, h->layers[0].attn_norm, nullptr))) return rc;
-  // attention partials hold tb_cap x n_kv x 1 split: n rows x nsb splits must fit
-  const int nsb = std::max(1, std::min(h->tb_attn_splits, h->tb_cap / n));
   if ((rc = tb_layers<BN>(h, n, tr, slot0, 0, nsb))) return rc;
   FinalNormParams fp{};
   fp.h = h->tb_h; fp.w = h->final_norm; fp.out = h->normed + (long long)slot0 * D; fp.D = D; fp.eps = h->cfg.norm_eps;
@@ -760,13 +758,29 @@ int enqueue_decode_batch_bn(vx_handle* h, int slot0, int n) {
   return VX_OK;
 }
 
+// Attention splits of a batched step: enough (slot, KV head, split) items for ~2
+// waves of 3 CTAs per SM once the context is long, at least 8 pages per split (at
+// short context one split per item, which writes its output without a merge).  The
+// partials hold tb_cap x n_kv x 1 split, so n rows x nsb splits must fit.
+// VX_BATCH_ATTN_SPLITS overrides.
+int batch_attn_splits(vx_handle* h, int slot0, int n) {
+  int max_pos = 0;
+  for (int s = slot0; s < slot0 + n; ++s) max_pos = std::max(max_pos, h->pos_host[s]);
+  const int pages = max_pos / kPage + 1;
+  const int want = h->tb_attn_splits > 0
+                       ? h->tb_attn_splits
+                       : std::max(1, std::min((6 * h->num_sms + h->NKV * n - 1) / (h->NKV * n), pages / 8));
+  return std::max(1, std::min({want, h->tb_cap / n, attn::kMaxSplits}));
+}
+
 int run_decode_batch(vx_handle* h, int slot0, int n) {
-  vx_handle::G& g = h->g_batch[((long long)slot0 << 20) | n];
+  const int nsb = batch_attn_splits(h, slot0, n);
+  vx_handle::G& g = h->g_batch[((long long)slot0 << 32) | ((long long)n << 8) | nsb];
   if (!g.exec) {
     cudaGraph_t graph;
     const long long before = h->launches;
     CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-    int rc = n <= 64 ? enqueue_decode_batch_bn<64>(h, slot0, n) : enqueue_decode_batch_bn<128>(h, slot0, n);
+    int rc = n <= 64 ? enqueue_decode_batch_bn<64>(h, slot0, n, nsb) : enqueue_decode_batch_bn<128>(h, slot0, n, nsb);
     cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
     if (rc) { if (ce == cudaSuccess) cudaGraphDestroy(graph); return rc; }
     if (ce != cudaSuccess) return h->fail(VX_E_CUDA, "graph capture: %s", cudaGetErrorString(ce));
@@ -1101,7 +1115,7 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   {
     const char* e = getenv("VX_NO_BATCHED_PREFILL");
     h->use_tb = h->tp == 1 && !(e && e[0] == '1');
-    if (const char* as = getenv("VX_BATCH_ATTN_SPLITS")) h->tb_attn_splits = std::max(1, std::min(8, atoi(as)));
+    if (const char* as = getenv("VX_BATCH_ATTN_SPLITS")) h->tb_attn_splits = std::max(1, std::min(64, atoi(as)));
     const char* tw = getenv("VX_PREFILL_TOKENWISE");
     h->prefill_tokenwise = tw && tw[0] == '1';
     if (h->use_tb && (rc = setup_tb(h))) { *out = h; return rc; }
@@ -1508,6 +1522,24 @@ int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm) {
   return VX_OK;
 }
 
+int vx_fill_kv(vx_handle* h, int32_t slot, int32_t n_positions, uint64_t seed) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (n_positions < 1 || n_positions > h->cfg.max_seq_len)
+    return h->fail(VX_E_RANGE, "n_positions %d outside [1, maxSeqLen %d]", n_positions, h->cfg.max_seq_len);
+  CK(cudaSetDevice(h->dev));
+  FillKvParams fp{h->kv_pool, h->page_table, slot, h->max_pages, h->L, h->NKV, h->rank * h->NKV,
+                  h->cfg.n_kv_heads * h->HD, n_positions, kPage, seed};
+  CK(launch(h, k_fill_kv_slot, dim3(16 * h->num_sms), dim3(256), 0, fp));
+  SlotUpdate u{};
+  u.set_counters = 1; u.pos = n_positions; u.frame = 0;
+  u.set_prompt_len = 1; u.prompt_len = n_positions;
+  if ((rc = slot_update(h, slot, u))) return rc;
+  h->pos_host[slot] = n_positions;
+  h->frame_host[slot] = 0;
+  return finish(h);
+}
+
 int vx_decode_batch(vx_handle* h, int32_t slot0, int32_t n_slots, int32_t n_frames) {
   if (!h) return VX_E_INVALID;
   int rc;
@@ -1534,13 +1566,13 @@ int vx_decode_batch(vx_handle* h, int32_t slot0, int32_t n_slots, int32_t n_fram
   }
   for (int f = 0; f < n_frames; ++f) {
     if ((rc = run_decode_batch(h, slot0, n_slots))) return rc;
+    for (int s = slot0; s < slot0 + n_slots; ++s) {
+      h->pos_host[s] += 1;
+      h->frame_host[s] += 1;
+    }
     if (f == 0 && any_kick)
       for (int s = slot0; s < slot0 + n_slots; ++s)
         if ((rc = set_slot_fields(h, s, kEmbSynthCodes, 0))) return rc;
-  }
-  for (int s = slot0; s < slot0 + n_slots; ++s) {
-    h->pos_host[s] += n_frames;
-    h->frame_host[s] += n_frames;
   }
   return VX_OK;
 }

@@ -92,6 +92,7 @@ def load_library():
         "vx_debug_layers": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p]),
         "vx_decode": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
         "vx_decode_batch": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+        "vx_fill_kv": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_uint64]),
         "vx_set_streams": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int32]),
         "vx_read_codes": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _u32p]),
         "vx_read_normed": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f32p]),
@@ -362,6 +363,11 @@ class VoxtralEngine:
         (tensor-core GEMMs over the slots); asynchronous."""
         self._require_ready()
         self._check(load_library().vx_decode_batch(self._h, slot0, n_slots, n_frames))
+
+    def fill_kv(self, n_positions: int, seed: int, slot: int = 0):
+        """Synthetic context: f16 N(0,1) K/V for positions [0, n_positions) of every layer."""
+        self._require_ready()
+        self._check(load_library().vx_fill_kv(self._h, slot, n_positions, seed))
 
     def read_codes(self, frame0: int, n: int, slot: int = 0) -> np.ndarray:
         out = np.empty((n, 37), np.uint32)
