@@ -222,6 +222,18 @@ int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, 
 int vx_nccl_unique_id(const char* nccl_lib, uint8_t out[128]);
 int vx_tp_init(vx_handle* h, const char* nccl_lib, const uint8_t id[128]);
 
+/* Tensor parallelism inside the persistent decode kernel (vx_decode / vx_prefill with
+ * tp_size > 1): the o_proj and down all-reduces of every layer run inside the kernel over
+ * peer memory (NVLink), instead of as NCCL calls between kernels.  Each rank exports the
+ * CUDA IPC handle (64 bytes) of its receive buffer with vx_tp_p2p_handle, the host
+ * gathers the tp_size handles in rank order (e.g. torch.distributed), and every rank
+ * passes them to vx_tp_p2p_open, then all ranks meet at a host barrier before their
+ * first decode.  All ranks must issue the same sequence of decode/prefill calls.  The
+ * reference runs on one device (src/engine.ts:814-1042); this is its step split over
+ * tp_size GPUs. */
+int vx_tp_p2p_handle(vx_handle* h, uint8_t out[64]);
+int vx_tp_p2p_open(vx_handle* h, const uint8_t* handles /* [tp_size][64] */);
+
 /* LM-head argmax for callers that cannot allocate device memory.  No counterpart in
  * the reference.  Callers that cannot call cudaMalloc (a real-time audio callback, where
  * cudaMalloc may synchronise the device and block; a host framework that owns all

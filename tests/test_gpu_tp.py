@@ -1,7 +1,9 @@
 """Tensor parallelism (batch-1 latency path) on 2 GPUs: q/KV heads and FFN columns sharded,
-NCCL all-reduce of the residual stream after o_proj and after down.  Both ranks must
-reproduce the golden fixture's per-layer tensors and FM outputs within the suite's
-tolerance.  Skipped when fewer than 2 GPUs are visible.  NVLS is disabled for the test."""
+all-reduce of the residual stream after o_proj and after down.  The per-step debug paths
+use NCCL between kernels; prefill and decode run the persistent kernel, whose all-reduces
+go through peer memory inside the kernel.  Both ranks must reproduce the golden fixture's
+per-layer tensors and FM outputs, and a backbone-only decode of the CPU oracle, within the
+suite's tolerance.  Skipped when fewer than 2 GPUs are visible.  NVLS is disabled."""
 import importlib
 import os
 import socket
@@ -10,9 +12,12 @@ import sys
 import numpy as np
 import pytest
 
+from conftest import max_abs_rel
+
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 TOL = 2e-2
+DEC_FRAMES = 8
 
 
 def _free_port() -> int:
@@ -42,6 +47,7 @@ def _rank_main(rank, world, port, q):
         torch.cuda.set_device(rank)
         vx = importlib.import_module("webgpu-voxtral_b200")
         vdist = importlib.import_module("webgpu-voxtral_b200.dist")
+        synth = importlib.import_module("webgpu-voxtral_b200.synth")
         vdist.init(backend="gloo", timeout_s=120)
         g = np.load(os.path.join(ROOT, "tests", "golden", "c1_small.npz"))
         eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 256, "maxFrames": 16,
@@ -58,7 +64,14 @@ def _rank_main(rank, world, port, q):
                     for i in range(kick.shape[0]))
         lrel = float(np.max(np.abs(f0["semantic_logits"] - g["f0_semantic_logits"])) /
                      np.max(np.abs(g["f0_semantic_logits"])))
-        q.put((rank, "ok", worst, lrel, f0["semantic_code"], int(g["f0_semantic_code"])))
+        # backbone-only decode through the tensor-parallel persistent kernel
+        toks, a0, na = synth.prompt(2, 150, 20)
+        eng.reset()
+        eng.set_streams(noise_seed=3, codes_seed=4, utt=6)
+        eng.prefill(toks, a0, na, synth.voice_rows(2, 20))
+        eng.decode(DEC_FRAMES, with_fm=False)
+        normed = eng.read_normed(0, DEC_FRAMES)
+        q.put((rank, "ok", worst, lrel, f0["semantic_code"], int(g["f0_semantic_code"]), normed))
         eng.destroy()
         vdist.barrier()
         vdist.shutdown()
@@ -83,8 +96,20 @@ def test_tp2_matches_golden():
         if p.is_alive():
             p.kill()
     for r in out:
-        assert r[1] == "ok", r
-        _, _, worst, lrel, sem, want = r
+        assert r[1] == "ok", r[:3]
+    import oracle
+    synth = importlib.import_module("webgpu-voxtral_b200.synth")
+    toks, a0, na = synth.prompt(2, 150, 20)
+    o = oracle.Oracle(n_layers=2, max_seq=256, with_fm=False)
+    ref = o.generate(toks, a0, na, synth.voice_rows(2, 20), DEC_FRAMES,
+                     codes_in=synth.feedback_codes(6, 0, DEC_FRAMES), want_normed=True)
+    o.close()
+    for r in out:
+        _, _, worst, lrel, sem, want, normed = r
         assert worst < TOL, worst
         assert lrel < TOL, lrel
         assert sem == want
+        for f in range(DEC_FRAMES):
+            assert max_abs_rel(normed[f], ref["normed"][f]) < TOL, (r[0], f)
+    # both ranks hold the same residual stream: identical outputs
+    assert np.array_equal(out[0][6], out[1][6])

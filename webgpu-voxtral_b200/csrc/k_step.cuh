@@ -21,6 +21,13 @@
 // Tiles of GEMV phase p are dealt round-robin starting at CTA (sum of earlier tile
 // counts) mod G, so every CTA's cumulative share of the weight stream stays within
 // one tile of the others.
+// Tensor parallelism (template degree N > 1, one kernel per GPU): each rank holds
+// 1/N of the q / KV heads and FFN columns.  The o_proj and down epilogues store the
+// rank's partial rows straight into every rank's receive buffer (peer memory over
+// NVLink) and arrive on per-source counters there; the next phase's prologue waits
+// for all ranks' arrivals and forms h = h_old + sum of the N partials in rank order,
+// so every rank holds the same residual stream (the reference's single-device step,
+// split over N GPUs with 2 all-reduces per layer fused into the kernel).
 // Every wait is bounded (vx_common.cuh): an expired wait records a device error and
 // the kernel unwinds instead of hanging.
 #pragma once
@@ -37,7 +44,21 @@ constexpr int kStages = 4;
 constexpr int kStageBytes = 36864;
 constexpr int kRedSlots = 4;
 constexpr int kMaxVals = 32;
-constexpr int D = 3072, QD = 4096, KVD = 1024, QKVD = 6144, F = 9216, HD = 128, NKV = 8, GQA = 4;
+constexpr int D = 3072, HD = 128, GQA = 4;
+constexpr int kMaxTp = 8;
+// Per-rank dimensions and tile geometry of tensor-parallel degree N.  O and W2
+// tiles keep ~32-36 KB per stage: RO / RW2 rows of the rank's K columns; WKO /
+// WKW2 consumer warps split K (8 / WK warps split the rows).
+template <int N>
+struct Tp {
+  static_assert(N == 1 || N == 2 || N == 4 || N == 8, "tensor-parallel degree");
+  static constexpr int QD = 4096 / N, KVD = 1024 / N, QKVD = QD + 2 * KVD, F = 9216 / N, NKV = 8 / N;
+  static constexpr int RO = 4 * N, WKO = N == 8 ? 4 : 8, CPLO = QD / 128 / WKO;
+  static constexpr int RW2 = 2 * N, WKW2 = 8 / N, CPLW2 = F / 128 / WKW2;
+  static constexpr int TQKV = QKVD / 6, TO = D / RO, TW13 = F / 3, TW2 = D / RW2;
+  static constexpr int TLayer = TQKV + TO + TW13 + TW2;
+  static_assert(RO * QD * 2 <= 36864 && RW2 * F * 2 <= 36864, "tile fits a stage");
+};
 
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int kOffRing = 0;
@@ -49,9 +70,6 @@ constexpr int kOffScratch = kOffRed + kRedSlots * kCW * kMaxVals * 4;
 constexpr int kScratchBytes = 4096;   // [0,256) combine weights / norm partials, [768,805) codes
 constexpr size_t kSmemBytes = (size_t)kOffScratch + kScratchBytes + 1024;   // + alignment slack
 
-// tiles per GEMV phase (rows per tile: QKV 6, O 4, W13 3 outputs, W2 2)
-constexpr int kTilesQKV = QKVD / 6, kTilesO = D / 4, kTilesW13 = F / 3, kTilesW2 = D / 2;
-constexpr int kTilesLayer = kTilesQKV + kTilesO + kTilesW13 + kTilesW2;
 // tiles per reduction group (group outputs TG * rows-per-tile <= 32)
 constexpr int kTgQKV = 1, kTgO = 1, kTgW13 = 1, kTgW2 = 1;
 
@@ -82,6 +100,14 @@ struct StepParams {
   int mode0, token0;      // embedding of the first step
   int mode_next;          // embedding of later steps
   int inc_frame, record;  // advance the frame counter / record normed states per step
+  // tensor parallelism (N > 1)
+  int rank;
+  float* h2;                          // second residual buffer (h alternates per all-reduce)
+  float* recv;                        // this rank's receive buffer [2 parity][N source][D]
+  float* peer_recv[kMaxTp];           // every rank's receive buffer (index = rank; own one included)
+  unsigned long long* arrive;         // this rank's arrival counters [N source] (monotonic)
+  unsigned long long* peer_arrive[kMaxTp];
+  unsigned long long ar_base;         // all-reduces completed before this launch
 };
 
 struct Smem {
@@ -132,10 +158,23 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+__device__ __forceinline__ unsigned long long ld_relaxed_sys64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_relaxed_sys_add64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 // Consumers (256 threads) wait until `target` CTA-phase arrivals are counted.  One
 // thread polls (relaxed loads, then one acquire fence); the named barrier releases
 // the others.  Writers publish with bar.sync + one red.release (no full fence).
-__device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid) {
+// With ar_target > 0 (tensor parallelism, after an all-reduce phase) the thread also
+// waits until every source rank's counter in p.arrive reaches ar_target (each of the
+// G CTAs of every rank arrives once per all-reduce), then fences at system scope.
+template <int N>
+__device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid,
+                                          unsigned long long ar_target = 0) {
   if (ctid == 0) {
     uint32_t i = 0;
     while (ld_relaxed(p.bar) < target) {
@@ -144,15 +183,39 @@ __device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, 
         break;
       }
     }
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    if (N > 1 && ar_target) {
+      for (int r = 0; r < N; ++r) {
+        uint32_t j = 0;
+        while (ld_relaxed_sys64(p.arrive + r) < ar_target) {
+          if (++j > (1u << 27) || ((j & 1023u) == 0 && error_set())) {
+            if (j > (1u << 27)) set_error(kDevTimeoutRed);
+            break;
+          }
+        }
+      }
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+    } else {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    }
   }
   named_bar_sync(1, kCW * 32);
 }
 // Arrival of this CTA for the current phase, by the warp that wrote its outputs.
-__device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, bool kv_written) {
+// peer: the warp stored partial rows into other ranks' memory.  The warp barrier
+// orders every lane's stores before lane 0's system-scope fence (cumulative, as the
+// CTA barrier + release of the local grid barrier); lane 0 then publishes to every
+// rank's counter for this source rank with relaxed reductions.
+template <int N>
+__device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, bool kv_written, bool peer = false) {
   if (kv_written) fence_proxy_async_global();   // KV rows (st.global) are read by TMA next phase
   __syncwarp();
-  if (lane == 0) red_release_add(p.bar, 1u);
+  if (lane == 0) {
+    red_release_add(p.bar, 1u);
+    if (N > 1 && peer) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int r = 0; r < N; ++r) red_relaxed_sys_add64(p.peer_arrive[r] + p.rank, 1ull);
+    }
+  }
 }
 // Phase trace (globaltimer ns) for the first kTraceFrames steps when p.trace is set:
 // [cta][phase][0] = consumers released, [1] = consumers done, [2] = epilogue arrival,
@@ -168,8 +231,10 @@ __device__ __forceinline__ int first_tile(int c, int off, int G) { return (c - o
 // ---------------------------------------------------------------- producer
 // Position in this CTA's sequence of weight tiles: (frame, layer, GEMV kind, tile).
 constexpr int kMaxPrefetchAhead = 32;   // bound on StepParams::prefetch_ahead
-__device__ __constant__ int kTilesOf[4] = {kTilesQKV, kTilesO, kTilesW13, kTilesW2};
-__device__ __constant__ int kTilePrefix[4] = {0, kTilesQKV, kTilesQKV + kTilesO, kTilesQKV + kTilesO + kTilesW13};
+template <int N>
+__device__ __forceinline__ int tiles_of(int k) {
+  return k == 0 ? Tp<N>::TQKV : k == 1 ? Tp<N>::TO : k == 2 ? Tp<N>::TW13 : Tp<N>::TW2;
+}
 struct Cursor {
   int f, l, k, t;
   int off;                    // dealing offset of the current phase: (tiles of earlier phases) mod G
@@ -179,9 +244,10 @@ __device__ __forceinline__ void cursor_layer(const StepParams& p, Cursor& x) {
   const LayerPtrs& W = p.layers[x.l];
   x.w0 = W.wqkv; x.w1 = W.wo; x.w2 = W.w13; x.w3 = W.w2;
 }
+template <int N>
 __device__ __forceinline__ void cursor_fix(const StepParams& p, Cursor& x, int c, int G, int L) {
-  while (x.t >= kTilesOf[x.k]) {
-    x.off = (x.off + kTilesOf[x.k]) % G;
+  while (x.t >= tiles_of<N>(x.k)) {
+    x.off = (x.off + tiles_of<N>(x.k)) % G;
     if (++x.k == 4) {
       x.k = 0;
       if (++x.l == L) { x.l = 0; ++x.f; }
@@ -190,24 +256,29 @@ __device__ __forceinline__ void cursor_fix(const StepParams& p, Cursor& x, int c
     x.t = first_tile(c, x.off, G);
   }
 }
+template <int N>
 __device__ __forceinline__ void cursor_start(const StepParams& p, Cursor& x, int c, int G, int L) {
   x.f = 0; x.l = 0; x.k = 0; x.off = 0; x.t = first_tile(c, 0, G);
   cursor_layer(p, x);
-  cursor_fix(p, x, c, G, L);
+  cursor_fix<N>(p, x, c, G, L);
 }
+template <int N>
 __device__ __forceinline__ void cursor_next(const StepParams& p, Cursor& x, int c, int G, int L) {
   x.t += G;
-  cursor_fix(p, x, c, G, L);
+  cursor_fix<N>(p, x, c, G, L);
 }
 // Source of a tile: first chunk (and the SwiGLU "up" chunk), bytes per chunk.
+// Every phase's row count is a multiple of its tile height, so tiles are full.
+template <int N>
 __device__ __forceinline__ void tile_src(const StepParams& p, const Cursor& x, const __half*& a, const __half*& b,
                                          uint32_t& bytes, int& ort) {
+  using T = Tp<N>;
   b = nullptr;
   switch (x.k) {
-    case 0: ort = 6; a = x.w0 + (long long)x.t * 6 * D; bytes = min(6, QKVD - x.t * 6) * D * 2; break;
-    case 1: ort = 4; a = x.w1 + (long long)x.t * 4 * QD; bytes = min(4, D - x.t * 4) * QD * 2; break;
-    case 2: ort = 3; a = x.w2 + (long long)x.t * 3 * D; b = a + (long long)F * D; bytes = min(3, F - x.t * 3) * D * 2; break;
-    default: ort = 2; a = x.w3 + (long long)x.t * 2 * F; bytes = min(2, D - x.t * 2) * F * 2; break;
+    case 0: ort = 6; a = x.w0 + (long long)x.t * 6 * D; bytes = 6 * D * 2; break;
+    case 1: ort = T::RO; a = x.w1 + (long long)x.t * T::RO * T::QD; bytes = T::RO * T::QD * 2; break;
+    case 2: ort = 3; a = x.w2 + (long long)x.t * 3 * D; b = a + (long long)T::F * D; bytes = 3 * D * 2; break;
+    default: ort = T::RW2; a = x.w3 + (long long)x.t * T::RW2 * T::F; bytes = T::RW2 * T::F * 2; break;
   }
 }
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
@@ -218,12 +289,25 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 // Tiles are consumed in groups of TG: each ring stage is released right after its
 // FMAs, but the cross-lane reduction, the reduction-slot handoff and the epilogue run
 // once per group (TG*R <= 32 outputs), which amortises their latency over TG tiles.
-template <int R, int CPL, bool NORM, int TG>
+// Inputs of a phase that follows a tensor-parallel all-reduce: the residual before
+// it (h_old), this rank's receive buffer of the all-reduce ([N source][D]) and the
+// buffer that receives h_old + sum of partials (written by CTA 0 only).
+struct ArIn {
+  const float* h_old;
+  const float* recv;
+  float* h_new;
+};
+// WK consumer warps split the tile's K columns (chunk j of warp (wr, wk) is
+// column block wk + WK*j), the 8/WK row groups split its R rows.
+template <int R, int CPL, bool NORM, int TG, int WK = kCW, int N = 1>
 __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& it, uint32_t& rit, const float* x,
                                        const __half* norm_w, int kc, int T, int off, int c, int G, int cw, int lane,
-                                       int pos, int f, int kl) {
-  static_assert(R * TG <= kMaxVals, "group too large");
-  constexpr int P = gemv::Pow2<R * TG>::v;
+                                       int pos, int f, int kl, const ArIn* ar = nullptr) {
+  constexpr int RW = R / (kCW / WK);   // rows per warp
+  static_assert(RW * (kCW / WK) == R && RW * TG <= kMaxVals, "tile rows");
+  static_assert(!NORM || WK == kCW, "RMSNorm phases partition the row over all warps");
+  constexpr int P = gemv::Pow2<RW * TG>::v;
+  const int wr = cw / WK, wk = cw % WK;
   // x' slice in registers.  For the RMSNorm variants each warp's slice (CPL x 128
   // columns; the 8 slices partition the row) also gives its partial sum of squares,
   // so the norm costs one load round and one named barrier.
@@ -232,8 +316,20 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
-    const int col = (cw + kCW * j) * 128 + lane * 4;
-    const float4 v = *reinterpret_cast<const float4*>(x + col);
+    const int col = (wk + WK * j) * 128 + lane * 4;
+    float4 v;
+    if (N > 1 && ar) {
+      // all-reduce: h = h_old + partials of ranks 0..N-1, the same order on every rank
+      v = __ldcg(reinterpret_cast<const float4*>(ar->h_old + col));
+#pragma unroll
+      for (int r = 0; r < N; ++r) {
+        const float4 q = __ldcg(reinterpret_cast<const float4*>(ar->recv + r * D + col));
+        v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+      }
+      if (c == 0) *reinterpret_cast<float4*>(ar->h_new + col) = v;
+    } else {
+      v = *reinterpret_cast<const float4*>(x + col);
+    }
     xr[j][0] = v.x; xr[j][1] = v.y; xr[j][2] = v.z; xr[j][3] = v.w;
     if (NORM) {
       const __half2* w2 = reinterpret_cast<const __half2*>(norm_w + col);
@@ -258,25 +354,26 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
   }
   trace_mark(p, c, f, kl, 3, p.n_layers, cw * 32 + lane);
   const int my_idx = gemv::transpose_index<P>(lane);
-  const bool writer = lane < P && my_idx < R * TG;
+  const bool writer = lane < P && my_idx < RW * TG;
   const uint32_t rowbytes = (uint32_t)kc * 2u;
   for (int g0 = first_tile(c, off, G); g0 < T; g0 += TG * G, ++rit) {
-    float acc[TG][R];
+    float acc[TG][RW];
 #pragma unroll
     for (int u = 0; u < TG; ++u)
 #pragma unroll
-      for (int r = 0; r < R; ++r) acc[u][r] = 0.f;
+      for (int r = 0; r < RW; ++r) acc[u][r] = 0.f;
 #pragma unroll
     for (int u = 0; u < TG; ++u) {
       if (g0 + u * G >= T) break;
       const int st = it % kStages;
       if (!mbar_wait(&s.full[st], (it / kStages) & 1u, kDevTimeoutFull)) return false;
-      const uint8_t* base = s.ring + (size_t)st * kStageBytes + (size_t)(cw * 128 + lane * 4) * 2;
+      const uint8_t* base =
+          s.ring + (size_t)st * kStageBytes + (size_t)(wk * 128 + lane * 4) * 2 + (size_t)(wr * RW) * rowbytes;
 #pragma unroll
-      for (int r = 0; r < R; ++r)
+      for (int r = 0; r < RW; ++r)
 #pragma unroll
         for (int j = 0; j < CPL; ++j) {
-          const uint2 wv = *reinterpret_cast<const uint2*>(base + (size_t)r * rowbytes + (size_t)j * kCW * 256);
+          const uint2 wv = *reinterpret_cast<const uint2*>(base + (size_t)r * rowbytes + (size_t)j * WK * 256);
           const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
           const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
           float a = acc[u][r];
@@ -292,7 +389,7 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
     }
     float v[P];
 #pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = i < R * TG ? acc[i / R][i % R] : 0.f;
+    for (int i = 0; i < P; ++i) v[i] = i < RW * TG ? acc[i / RW][i % RW] : 0.f;
     const float rv = gemv::transpose_reduce<P>(v, lane);
     const int rs = rit % kRedSlots;
     if (!mbar_wait(&s.rempty[rs], ((rit / kRedSlots) & 1u) ^ 1u, kDevTimeoutRed)) return false;
@@ -305,10 +402,16 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
 
 // ---------------------------------------------------------------- epilogue GEMV phase
 // EPI: gemv::kQkv (rows -> q / K / V with RoPE), kResid (y += ), kSwiglu (g = silu(a)*b)
-template <int R, int EPI, int TG>
+// kPeer (tensor parallelism): the tile's rows are this rank's partial of an
+// all-reduce; they are stored into every rank's receive buffer (slot `rank` of
+// parity `par`) and summed by the next phase's prologue.
+constexpr int kPeer = 100;
+template <int R, int EPI, int TG, int WK = kCW, int N = 1>
 __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t& rit, float* y, int rows, int T,
-                                         int off, int c, int G, int lane, int layer, int pos) {
+                                         int off, int c, int G, int lane, int layer, int pos, int par = 0) {
+  using TD = Tp<N>;
   constexpr int ORT = EPI == gemv::kSwiglu ? R / 2 : R;
+  constexpr int RW = R / (kCW / WK);
   for (int g0 = first_tile(c, off, G); g0 < T; g0 += TG * G, ++rit) {
     const int rs = rit % kRedSlots;
     // lane -> (tile u of the group, row r of the tile)
@@ -323,12 +426,19 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
     if (!mbar_wait(&s.rfull[rs], (rit / kRedSlots) & 1u, kDevTimeoutRed)) return false;
     float val = 0.f;
     if (lane < R * TG) {
+      // row r of tile u: written by the WK warps of row group r / RW at index u*RW + r%RW
+      const int wr = r / RW, idx = u * RW + r % RW;
 #pragma unroll
-      for (int w = 0; w < kCW; ++w) val += s.red[(rs * kCW + w) * kMaxVals + lane];
+      for (int k = 0; k < WK; ++k) val += s.red[(rs * kCW + wr * WK + k) * kMaxVals + idx];
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.rempty[rs]);
-    if constexpr (EPI == gemv::kResid) {
+    if constexpr (EPI == kPeer) {
+      const int row = t * R + r;
+      if (live && row < rows)
+#pragma unroll
+        for (int q = 0; q < N; ++q) p.peer_recv[q][((long long)par * N + p.rank) * D + row] = val;
+    } else if constexpr (EPI == gemv::kResid) {
       const int row = t * ORT + r;
       if (live && row < rows) y[row] = yold + val;
     } else if constexpr (EPI == gemv::kSwiglu) {
@@ -340,7 +450,7 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
       const int row = t * R + r;
       if (live && row < rows) {
         float out = val;
-        if (row < QD + KVD) {
+        if (row < TD::QD + TD::KVD) {
           const float ang = (float)pos * p.rope_freq[(row & 127) >> 1];
           float sn, cs;
           sincosf(ang, &sn, &cs);
@@ -348,12 +458,12 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
           const float x0 = even ? val : other, x1 = even ? other : val;
           out = even ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
         }
-        if (row < QD) {
+        if (row < TD::QD) {
           p.q[row] = out;
         } else {
-          const int kvr = row - QD;
-          const int kv = kvr >= KVD ? 1 : 0;
-          const int rr = kvr - kv * KVD;
+          const int kvr = row - TD::QD;
+          const int kv = kvr >= TD::KVD ? 1 : 0;
+          const int rr = kvr - kv * TD::KVD;
           const int lp = pos / p.kv.page_size;
           if (lp >= p.kv.max_pages) {
             set_error(kDevBadIndex);
@@ -366,7 +476,7 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
       }
     }
   }
-  grid_arrive_warp(p, lane, EPI == gemv::kQkv);
+  grid_arrive_warp<N>(p, lane, EPI == gemv::kQkv, EPI == kPeer);
   return true;
 }
 
@@ -404,9 +514,10 @@ __device__ __forceinline__ void issue_pair(const StepParams& p, const CUtensorMa
 // Called at the start of the QKV phase: the first page pair of this CTA's attention
 // item holds only positions written by earlier steps (except the current position's
 // row, patched in the attention phase), so its TMA can run under the QKV phase.
+template <int N>
 __device__ __forceinline__ bool prestage(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int pos,
                                          int c, int ctid, bool& a_pending) {
-  if (!p.prestage_kv || c >= NKV * p.n_splits) return false;
+  if (!p.prestage_kv || c >= Tp<N>::NKV * p.n_splits) return false;
   int npages, pps, n_used;
   split_plan(p, pos, npages, pps, n_used);
   const int kvh = c / p.n_splits, split = c % p.n_splits;
@@ -421,6 +532,7 @@ __device__ __forceinline__ bool prestage(const StepParams& p, const CUtensorMap*
 
 // Control flow is uniform across the 256 consumer threads (every named barrier is
 // reached by all of them); after a device error the work is skipped, not the barriers.
+template <int N>
 __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap* kvmap, Smem& s, uint32_t& ait,
                                           bool& a_pending, bool staged, int layer, int pos, int c, int G, int cw,
                                           int lane, int ctid) {
@@ -432,7 +544,7 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
   const int g = lane >> 2, hq = g & 3;
   const bool lo_part = g >= 4;
   const int half_pair = cw >> 2, grp = cw & 3;
-  for (int item = c; item < NKV * p.n_splits; item += G) {
+  for (int item = c; item < Tp<N>::NKV * p.n_splits; item += G) {
     const int kvh = item / p.n_splits, split = item % p.n_splits;
     if (split >= n_used) continue;   // uniform: no positions in this split
     const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
@@ -649,8 +761,10 @@ __device__ __forceinline__ int embed_source(const StepParams& p, int mode, int t
 }
 
 // ---------------------------------------------------------------- the kernel
+template <int N>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_constant__ CUtensorMap kvmap,
                                                               const __grid_constant__ StepParams p) {
+  using TD = Tp<N>;
   extern __shared__ uint8_t smem_raw[];
   Smem s = smem_map(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -673,31 +787,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       const uint64_t pol = policy_evict_first();
       uint32_t it = 0;
       Cursor cur, ahead;
-      cursor_start(p, cur, c, G, L);
-      cursor_start(p, ahead, c, G, L);
+      cursor_start<N>(p, cur, c, G, L);
+      cursor_start<N>(p, ahead, c, G, L);
       for (int i = 0; i < p.prefetch_ahead && ahead.f < p.n_frames; ++i) {
         const __half *a, *b; uint32_t bytes; int ort;
-        tile_src(p, ahead, a, b, bytes, ort);
+        tile_src<N>(p, ahead, a, b, bytes, ort);
         prefetch_l2(a, bytes);
         if (b) prefetch_l2(b, bytes);
-        cursor_next(p, ahead, c, G, L);
+        cursor_next<N>(p, ahead, c, G, L);
       }
       while (cur.f < p.n_frames) {
         const int st = it % kStages;
         if (!mbar_wait(&s.empty[st], ((it / kStages) & 1u) ^ 1u, kDevTimeoutEmpty)) break;
         const __half *a, *b; uint32_t bytes; int ort;
-        tile_src(p, cur, a, b, bytes, ort);
+        tile_src<N>(p, cur, a, b, bytes, ort);
         mbar_arrive_expect_tx(&s.full[st], bytes * (b ? 2u : 1u));
         uint8_t* dst = s.ring + (size_t)st * kStageBytes;
         bulk_g2s(dst, a, bytes, &s.full[st], pol);
         if (b) bulk_g2s(dst + (size_t)ort * D * 2, b, bytes, &s.full[st], pol);   // SwiGLU up rows after the gate rows
         ++it;
-        cursor_next(p, cur, c, G, L);
+        cursor_next<N>(p, cur, c, G, L);
         if (p.prefetch_ahead > 0 && ahead.f < p.n_frames) {
-          tile_src(p, ahead, a, b, bytes, ort);
+          tile_src<N>(p, ahead, a, b, bytes, ort);
           prefetch_l2(a, bytes);
           if (b) prefetch_l2(b, bytes);
-          cursor_next(p, ahead, c, G, L);
+          cursor_next<N>(p, ahead, c, G, L);
         }
       }
       // drain the copies still in flight
@@ -714,21 +828,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     long long tiles_before = 0;
     for (int f = 0; f < p.n_frames; ++f) {
       const int pos = pos0 + f;
+      const unsigned long long kf = p.ar_base + 2ull * L * f;   // all-reduce index of layer 0's o_proj
       for (int l = 0; l < L; ++l) {
         const int o0 = (int)(tiles_before % G);
-        const int o1 = (int)((tiles_before + kTilesQKV) % G);
-        const int o2 = (int)((tiles_before + kTilesQKV + kTilesO) % G);
-        const int o3 = (int)((tiles_before + kTilesQKV + kTilesO + kTilesW13) % G);
+        const int o1 = (int)((tiles_before + TD::TQKV) % G);
+        const int o2 = (int)((tiles_before + TD::TQKV + TD::TO) % G);
+        const int o3 = (int)((tiles_before + TD::TQKV + TD::TO + TD::TW13) % G);
         const int kl = 1 + 5 * l;
-        if (!epilogue<6, gemv::kQkv, kTgQKV>(p, s, rit, nullptr, QKVD, kTilesQKV, o0, c, G, lane, l, pos)) return;
+        const int par_o = (int)((kf + 2 * l) & 1), par_w2 = (int)((kf + 2 * l + 1) & 1);
+        if (!epilogue<6, gemv::kQkv, kTgQKV, kCW, N>(p, s, rit, nullptr, TD::QKVD, TD::TQKV, o0, c, G, lane, l, pos))
+          return;
         trace_mark(p, c, f, kl, 2, L, lane);
-        if (!epilogue<4, gemv::kResid, kTgO>(p, s, rit, p.h, D, kTilesO, o1, c, G, lane, l, pos)) return;
+        if constexpr (N == 1) {
+          if (!epilogue<4, gemv::kResid, kTgO>(p, s, rit, p.h, D, TD::TO, o1, c, G, lane, l, pos)) return;
+        } else {
+          if (!epilogue<TD::RO, kPeer, 1, TD::WKO, N>(p, s, rit, nullptr, D, TD::TO, o1, c, G, lane, l, pos, par_o))
+            return;
+        }
         trace_mark(p, c, f, kl + 2, 2, L, lane);
-        if (!epilogue<6, gemv::kSwiglu, kTgW13>(p, s, rit, p.g, F, kTilesW13, o2, c, G, lane, l, pos)) return;
+        if (!epilogue<6, gemv::kSwiglu, kTgW13, kCW, N>(p, s, rit, p.g, TD::F, TD::TW13, o2, c, G, lane, l, pos)) return;
         trace_mark(p, c, f, kl + 3, 2, L, lane);
-        if (!epilogue<2, gemv::kResid, kTgW2>(p, s, rit, p.h, D, kTilesW2, o3, c, G, lane, l, pos)) return;
+        if constexpr (N == 1) {
+          if (!epilogue<2, gemv::kResid, kTgW2>(p, s, rit, p.h, D, TD::TW2, o3, c, G, lane, l, pos)) return;
+        } else {
+          if (!epilogue<TD::RW2, kPeer, 1, TD::WKW2, N>(p, s, rit, nullptr, D, TD::TW2, o3, c, G, lane, l, pos, par_w2))
+            return;
+        }
         trace_mark(p, c, f, kl + 4, 2, L, lane);
-        tiles_before += kTilesLayer;
+        tiles_before += TD::TLayer;
       }
     }
     return;
@@ -743,10 +870,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   const int e0 = c * per, e1 = min(D, e0 + per);
   uint32_t* codes = reinterpret_cast<uint32_t*>(s.scratch + 768);
   bool a_pending = false;   // an attention TMA pair is in flight (thread 0)
+  // tensor parallelism: the residual alternates between p.h and p.h2 per all-reduce
+  // (all-reduce k reads h[k & 1] and its parity k & 1 of the receive buffer, writes
+  // h[(k + 1) & 1]); every launch starts at an even all-reduce index, so EMBED
+  // writes p.h and the last all-reduce of a launch leaves the residual in p.h.
+  float* const hb[2] = {p.h, N > 1 ? p.h2 : p.h};
+  auto ar_in = [&](unsigned long long k) {
+    return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1]};
+  };
   for (int f = 0; f < p.n_frames; ++f) {
     const int pos = pos0 + f, frame = frame0 + f;
+    const unsigned long long kf = p.ar_base + 2ull * L * f;
     // ---- EMBED
-    grid_wait(p, phase * G, ctid);
+    grid_wait<N>(p, phase * G, ctid);
     trace_mark(p, c, f, 0, 0, L, ctid);
     {
       int row = 0, kind = -1;
@@ -790,50 +926,76 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     for (int l = 0; l < L; ++l) {
       const LayerPtrs& W = p.layers[l];
       const int o0 = (int)(tiles_before % G);
-      const int o1 = (int)((tiles_before + kTilesQKV) % G);
-      const int o2 = (int)((tiles_before + kTilesQKV + kTilesO) % G);
-      const int o3 = (int)((tiles_before + kTilesQKV + kTilesO + kTilesW13) % G);
+      const int o1 = (int)((tiles_before + TD::TQKV) % G);
+      const int o2 = (int)((tiles_before + TD::TQKV + TD::TO) % G);
+      const int o3 = (int)((tiles_before + TD::TQKV + TD::TO + TD::TW13) % G);
       const int kl = 1 + 5 * l;
-      // ---- QKV (+ RoPE + KV append in the epilogue warp)
-      grid_wait(p, phase * G, ctid);
+      const unsigned long long k_o = kf + 2 * l, k_prev = kf + 2 * l - 1;   // k_prev: layer l-1's down
+      // ---- QKV (+ RoPE + KV append in the epilogue warp); TP: h = all-reduce of layer l-1's down
+      const bool ar_qkv = N > 1 && l > 0;
+      grid_wait<N>(p, phase * G, ctid, ar_qkv ? (k_prev + 1) * G : 0ull);
       trace_mark(p, c, f, kl, 0, L, ctid);
-      const bool staged = prestage(p, &kvmap, s, l, pos, c, ctid, a_pending);
-      consume<6, 3, true, kTgQKV>(p, s, it, rit, p.h, W.attn_norm, D, kTilesQKV, o0, c, G, cw, lane, pos, f, kl);
+      const bool staged = prestage<N>(p, &kvmap, s, l, pos, c, ctid, a_pending);
+      {
+        const ArIn a = ar_qkv ? ar_in(k_prev) : ArIn{};
+        consume<6, 3, true, kTgQKV, kCW, N>(p, s, it, rit, hb[0], W.attn_norm, D, TD::TQKV, o0, c, G, cw, lane, pos, f,
+                                            kl, ar_qkv ? &a : nullptr);
+      }
       trace_mark(p, c, f, kl, 1, L, ctid);
       ++phase;
       // ---- attention
-      grid_wait(p, phase * G, ctid);
+      grid_wait<N>(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 1, 0, L, ctid);
-      attention(p, &kvmap, s, ait, a_pending, staged, l, pos, c, G, cw, lane, ctid);
+      attention<N>(p, &kvmap, s, ait, a_pending, staged, l, pos, c, G, cw, lane, ctid);
       trace_mark(p, c, f, kl + 1, 1, L, ctid);
       if (ctid == 0) red_release_add(p.bar, 1u);
       ++phase;
-      // ---- o_proj + residual
-      grid_wait(p, phase * G, ctid);
+      // ---- o_proj + residual (TP: partial rows to every rank)
+      grid_wait<N>(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 2, 0, L, ctid);
-      consume<4, 4, false, kTgO>(p, s, it, rit, p.att, nullptr, QD, kTilesO, o1, c, G, cw, lane, pos, f, kl + 2);
+      consume<TD::RO, TD::CPLO, false, kTgO, TD::WKO, N>(p, s, it, rit, p.att, nullptr, TD::QD, TD::TO, o1, c, G, cw,
+                                                         lane, pos, f, kl + 2);
       trace_mark(p, c, f, kl + 2, 1, L, ctid);
       ++phase;
-      // ---- gate/up + SwiGLU
-      grid_wait(p, phase * G, ctid);
+      // ---- gate/up + SwiGLU; TP: h = all-reduce of o_proj
+      grid_wait<N>(p, phase * G, ctid, N > 1 ? (k_o + 1) * G : 0ull);
       trace_mark(p, c, f, kl + 3, 0, L, ctid);
-      consume<6, 3, true, kTgW13>(p, s, it, rit, p.h, W.ffn_norm, D, kTilesW13, o2, c, G, cw, lane, pos, f, kl + 3);
+      {
+        const ArIn a = N > 1 ? ar_in(k_o) : ArIn{};
+        consume<6, 3, true, kTgW13, kCW, N>(p, s, it, rit, hb[0], W.ffn_norm, D, TD::TW13, o2, c, G, cw, lane, pos, f,
+                                            kl + 3, N > 1 ? &a : nullptr);
+      }
       trace_mark(p, c, f, kl + 3, 1, L, ctid);
       ++phase;
-      // ---- down + residual
-      grid_wait(p, phase * G, ctid);
+      // ---- down + residual (TP: partial rows to every rank)
+      grid_wait<N>(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 4, 0, L, ctid);
-      consume<2, 9, false, kTgW2>(p, s, it, rit, p.g, nullptr, F, kTilesW2, o3, c, G, cw, lane, pos, f, kl + 4);
+      consume<TD::RW2, TD::CPLW2, false, kTgW2, TD::WKW2, N>(p, s, it, rit, p.g, nullptr, TD::F, TD::TW2, o3, c, G, cw,
+                                                             lane, pos, f, kl + 4);
       trace_mark(p, c, f, kl + 4, 1, L, ctid);
       ++phase;
-      tiles_before += kTilesLayer;
+      tiles_before += TD::TLayer;
     }
-    // ---- FINAL norm (each CTA: full sum of squares, its slice of the output)
-    grid_wait(p, phase * G, ctid);
+    // ---- FINAL norm (each CTA: full sum of squares, its slice of the output);
+    // TP: h = all-reduce of the last layer's down (CTA 0 stores it to p.h)
+    const unsigned long long k_last = kf + 2ull * L - 1;
+    grid_wait<N>(p, phase * G, ctid, N > 1 ? (k_last + 1) * G : 0ull);
     trace_mark(p, c, f, 1 + 5 * L, 0, L, ctid);
     {
+      const ArIn fa = N > 1 ? ar_in(k_last) : ArIn{};
+      auto hval = [&](int i) -> float {
+        if (N == 1) return p.h[i];
+        float v = __ldcg(fa.h_old + i);
+#pragma unroll
+        for (int r = 0; r < N; ++r) v += __ldcg(fa.recv + r * D + i);
+        return v;
+      };
       float ss = 0.f;
-      for (int i = ctid; i < D; i += kCW * 32) ss += p.h[i] * p.h[i];
+      for (int i = ctid; i < D; i += kCW * 32) {
+        const float v = hval(i);
+        ss += v * v;
+        if (N > 1 && c == 0) fa.h_new[i] = v;
+      }
       ss = warp_sum(ss);
       if (lane == 0) s.scratch[cw] = ss;
       named_bar_sync(1, kCW * 32);
@@ -845,7 +1007,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       float* ring = (p.record && frame >= 0 && frame < st.max_frames)
                         ? p.normed_ring + ((long long)p.slot * st.max_frames + frame) * D : nullptr;
       for (int i = e0 + ctid; i < e1; i += kCW * 32) {
-        const float v = p.h[i] * rms * __half2float(p.final_norm[i]);
+        const float v = hval(i) * rms * __half2float(p.final_norm[i]);
         p.normed[i] = v;
         if (ring) ring[i] = v;
       }
@@ -858,7 +1020,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   if (ctid == 0 && a_pending) mbar_wait(s.afull, (ait - 1) & 1u, kDevTimeoutDrain);
   // slot bookkeeping once every CTA has finished the last step
   if (c == 0) {
-    grid_wait(p, phase * G, ctid);
+    grid_wait<N>(p, phase * G, ctid);
     if (ctid == 0 && !error_set()) {
       SlotState& st = p.slots[p.slot];
       st.pos = pos0 + p.n_frames;

@@ -145,6 +145,14 @@ struct vx_handle {
 
   // TP
   ncclComm_t comm = nullptr;
+  // TP persistent kernel: receive buffers + arrival counters in peer-accessible memory
+  // (CUDA IPC), the residual's second buffer, and all-reduces completed so far
+  void* p2p_buf = nullptr;
+  void* p2p_peer[mk::kMaxTp] = {nullptr};
+  bool p2p_ready = false;
+  float* h2 = nullptr;
+  unsigned long long ar_base = 0;
+  bool coop = false;
 
   // persistent decode kernel (k_step.cuh): layer table and grid-barrier counter
   bool use_mk = true;
@@ -238,13 +246,21 @@ int prime_kernel_attrs(vx_handle* h) {
   CK(gemv_attr<6, 4, 3, kSwiglu, true>()); CK(gemv_attr<6, 4, 3, kResid, false>());
   CK(gemv_attr<2, 6, 3, kStore, true>());
   CK(cudaFuncSetAttribute(attn::k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn::kSmemBytes));
-  CK(cudaFuncSetAttribute(mk::k_decode_steps, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
   CK(tc_attr<64>()); CK(tc_attr<128>()); CK(tc_attr<256>());
   return VX_OK;
 }
 
 // n_frames consecutive backbone steps of one slot in ONE cooperative launch of the
 // persistent decode kernel (k_step.cuh).
+// Peer-accessible block of the TP persistent kernel: receive buffers [2][tp][D]
+// floats, then one 64-bit arrival counter per source rank.
+constexpr size_t kP2pCounterOff = 256 * 1024;
+constexpr size_t kP2pBytes = kP2pCounterOff + 4096;
+
 int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, int mode_next, bool inc_frame,
                  bool record) {
   if (n_frames <= 0) return VX_OK;
@@ -279,8 +295,26 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  if (h->tp > 1) {
+    if (!h->p2p_ready) return h->fail(VX_E_STATE, "tensor-parallel persistent kernel needs vx_tp_p2p_open");
+    sp.rank = h->rank;
+    sp.h2 = h->h2 + slot * D;
+    sp.recv = reinterpret_cast<float*>(h->p2p_buf);
+    sp.arrive = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(h->p2p_buf) + kP2pCounterOff);
+    for (int r = 0; r < h->tp; ++r) {
+      sp.peer_recv[r] = reinterpret_cast<float*>(h->p2p_peer[r]);
+      sp.peer_arrive[r] = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(h->p2p_peer[r]) + kP2pCounterOff);
+    }
+    sp.ar_base = h->ar_base;
+  }
   h->launches++;
-  CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps, h->kv_map, sp));
+  switch (h->tp) {
+    case 1: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<1>, h->kv_map, sp)); break;
+    case 2: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<2>, h->kv_map, sp)); break;
+    case 4: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<4>, h->kv_map, sp)); break;
+    default: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<8>, h->kv_map, sp)); break;
+  }
+  if (h->tp > 1) h->ar_base += 2ull * h->L * (unsigned long long)n_frames;
   return VX_OK;
 }
 
@@ -1010,6 +1044,7 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   auto f32n = [&](size_t n) { act += ((n * 4 + 255) & ~size_t(255)); };
   f32n(64);  // rope
   f32n((size_t)h->B * D * 3 + (size_t)h->B * h->QD * 2 + (size_t)h->B * h->Fl);
+  f32n((size_t)h->B * D);  // h2
   f32n((size_t)h->B * h->NKV * h->n_splits * attn::kGqa * attn::kPartStride);
   f32n((size_t)h->B * h->NKV);
   f32n((size_t)h->B * c.max_seq_len);
@@ -1041,6 +1076,7 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   auto fa = [&](size_t n) { return (float*)carve(ac, n * 4); };
   h->rope_freq = fa(64);
   h->h = fa((size_t)h->B * D); h->normed = fa((size_t)h->B * D); h->rows_in = fa((size_t)h->B * D);
+  h->h2 = fa((size_t)h->B * D);
   h->q = fa((size_t)h->B * h->QD); h->att = fa((size_t)h->B * h->QD); h->g = fa((size_t)h->B * h->Fl);
   h->attn_part = fa((size_t)h->B * h->NKV * h->n_splits * attn::kGqa * attn::kPartStride);
   h->attn_tickets = (int*)fa((size_t)h->B * h->NKV);
@@ -1110,7 +1146,8 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     if (const char* pa = getenv("VX_PREFETCH_AHEAD")) h->prefetch_ahead = std::max(0, std::min(mk::kMaxPrefetchAhead, atoi(pa)));
     if (const char* ps = getenv("VX_PRESTAGE_KV")) h->prestage_kv = atoi(ps) != 0;
     const char* e = getenv("VX_NO_MEGAKERNEL");
-    h->use_mk = coop && h->tp == 1 && !(e && e[0] == '1');
+    h->coop = coop != 0 && !(e && e[0] == '1');
+    h->use_mk = h->coop && h->tp == 1;   // TP: enabled by vx_tp_p2p_open
   }
   {
     const char* e = getenv("VX_NO_BATCHED_PREFILL");
@@ -1134,6 +1171,9 @@ void vx_destroy(vx_handle* h) {
   for (auto& kv : h->g_batch)
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
   if (h->comm && g_nccl.commDestroy) g_nccl.commDestroy(h->comm);
+  for (int r = 0; r < mk::kMaxTp; ++r)
+    if (h->p2p_peer[r] && h->p2p_peer[r] != h->p2p_buf) cudaIpcCloseMemHandle(h->p2p_peer[r]);
+  if (h->p2p_buf) cudaFree(h->p2p_buf);
   if (h->arena) cudaFree(h->arena);
   if (h->d_layers) cudaFree(h->d_layers);
   if (h->d_trace) cudaFree(h->d_trace);
@@ -1724,6 +1764,40 @@ int vx_tp_init(vx_handle* h, const char* lib, const uint8_t id_bytes[128]) {
   memcpy(id.internal, id_bytes, 128);
   ncclResult_t r = g_nccl.commInitRank(&h->comm, h->tp, id, h->rank);
   if (r != ncclSuccess) return h->fail(VX_E_NCCL, "ncclCommInitRank: %s", g_nccl.getErrorString(r));
+  return VX_OK;
+}
+
+int vx_tp_p2p_handle(vx_handle* h, uint8_t out[64]) {
+  if (!h || !out) return VX_E_INVALID;
+  if (h->tp < 2) return h->fail(VX_E_STATE, "tp_size is 1");
+  CK(cudaSetDevice(h->dev));
+  if (!h->p2p_buf) {
+    CK(cudaMalloc(&h->p2p_buf, kP2pBytes));
+    CK(cudaMemset(h->p2p_buf, 0, kP2pBytes));   // arrival counters start at zero on every rank
+    CK(cudaDeviceSynchronize());
+  }
+  cudaIpcMemHandle_t mh;
+  CK(cudaIpcGetMemHandle(&mh, h->p2p_buf));
+  static_assert(sizeof(mh) == 64, "IPC handle size");
+  memcpy(out, &mh, 64);
+  return VX_OK;
+}
+
+int vx_tp_p2p_open(vx_handle* h, const uint8_t* handles) {
+  if (!h || !handles) return VX_E_INVALID;
+  if (h->tp < 2 || !h->p2p_buf) return h->fail(VX_E_STATE, "call vx_tp_p2p_handle first");
+  CK(cudaSetDevice(h->dev));
+  for (int r = 0; r < h->tp; ++r) {
+    if (r == h->rank) { h->p2p_peer[r] = h->p2p_buf; continue; }
+    if (h->p2p_peer[r]) continue;
+    cudaIpcMemHandle_t mh;
+    memcpy(&mh, handles + 64 * r, 64);
+    void* ptr = nullptr;
+    CK(cudaIpcOpenMemHandle(&ptr, mh, cudaIpcMemLazyEnablePeerAccess));
+    h->p2p_peer[r] = ptr;
+  }
+  h->p2p_ready = true;
+  h->use_mk = h->coop;
   return VX_OK;
 }
 

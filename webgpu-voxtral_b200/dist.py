@@ -73,6 +73,15 @@ def broadcast_bytes(payload: Optional[bytes], src: int = 0) -> bytes:
     return obj[0]
 
 
+def all_gather_bytes(payload: bytes) -> list:
+    """Every rank's byte string, in rank order (e.g. 64-byte CUDA IPC handles)."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return [payload]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, payload)
+    return out
+
+
 def shutdown():
     if dist.is_available() and dist.is_initialized():
         dist.destroy_process_group()

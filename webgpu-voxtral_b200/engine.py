@@ -108,6 +108,8 @@ def load_library():
                                             ctypes.c_int32, ctypes.c_uint64, ctypes.POINTER(ctypes.c_double)]),
         "vx_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p, _u8p]),
         "vx_tp_init": (ctypes.c_int, [H, ctypes.c_char_p, _u8p]),
+        "vx_tp_p2p_handle": (ctypes.c_int, [H, _u8p]),
+        "vx_tp_p2p_open": (ctypes.c_int, [H, _u8p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -476,6 +478,17 @@ def nccl_unique_id(nccl_lib: Optional[str] = None) -> bytes:
     return bytes(buf)
 
 
-def tp_init(engine: VoxtralEngine, uid: bytes, nccl_lib: Optional[str] = None):
+def tp_init(engine: VoxtralEngine, uid: bytes, nccl_lib: Optional[str] = None, p2p: bool = True):
+    """Tensor-parallel set-up of one rank: NCCL (per-op path) and, with p2p, the peer-memory
+    all-reduce of the persistent decode kernel (IPC handles exchanged with torch.distributed;
+    ends with a barrier so no rank starts decoding before every rank's buffers are open)."""
     buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
-    engine._check(load_library().vx_tp_init(engine.handle, nccl_lib.encode() if nccl_lib else None, buf))
+    L = load_library()
+    engine._check(L.vx_tp_init(engine.handle, nccl_lib.encode() if nccl_lib else None, buf))
+    if p2p:
+        from . import dist as vdist
+        mine = (ctypes.c_uint8 * 64)()
+        engine._check(L.vx_tp_p2p_handle(engine.handle, mine))
+        allh = b"".join(vdist.all_gather_bytes(bytes(mine)))
+        engine._check(L.vx_tp_p2p_open(engine.handle, (ctypes.c_uint8 * len(allh)).from_buffer_copy(allh)))
+        vdist.barrier()
