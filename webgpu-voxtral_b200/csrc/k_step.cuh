@@ -24,10 +24,12 @@
 // Tensor parallelism (template degree N > 1, one kernel per GPU): each rank holds
 // 1/N of the q / KV heads and FFN columns.  The o_proj and down epilogues store the
 // rank's partial rows straight into every rank's receive buffer (peer memory over
-// NVLink) and arrive on per-source counters there; the next phase's prologue waits
-// for all ranks' arrivals and forms h = h_old + sum of the N partials in rank order,
-// so every rank holds the same residual stream (the reference's single-device step,
-// split over N GPUs with 2 all-reduces per layer fused into the kernel).
+// NVLink) as 8-byte words {value, all-reduce index + 1}; the next phase's prologue
+// polls those words until every rank's tag has arrived (no fence, no counter, no
+// grid barrier on this transition) and forms h = h_old + sum of the N partials in
+// rank order, so every rank holds the same residual stream (the reference's
+// single-device step, split over N GPUs with 2 all-reduces per layer fused into the
+// kernel).
 // Every wait is bounded (vx_common.cuh): an expired wait records a device error and
 // the kernel unwinds instead of hanging.
 #pragma once
@@ -103,10 +105,8 @@ struct StepParams {
   // tensor parallelism (N > 1)
   int rank;
   float* h2;                          // second residual buffer (h alternates per all-reduce)
-  float* recv;                        // this rank's receive buffer [2 parity][N source][D]
-  float* peer_recv[kMaxTp];           // every rank's receive buffer (index = rank; own one included)
-  unsigned long long* arrive;         // this rank's arrival counters [N source] (monotonic)
-  unsigned long long* peer_arrive[kMaxTp];
+  unsigned long long* recv;           // this rank's receive words [2 parity][N source][D]: tag << 32 | f32 bits
+  unsigned long long* peer_recv[kMaxTp];   // every rank's receive words (index = rank; own one included)
   unsigned long long ar_base;         // all-reduces completed before this launch
 };
 
@@ -158,24 +158,60 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ unsigned long long ld_relaxed_sys64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+// Tagged all-reduce words: 8-byte single-copy-atomic stores / loads, so a reader
+// that sees the expected tag also sees the value stored with it.
+__device__ __forceinline__ void st_tagged(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_tagged2(const unsigned long long* p) {
+  ulonglong2 v;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void red_relaxed_sys_add64(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Value of a tagged word once its tag is `tag` (bounded poll: an expired wait records
+// an error and returns the word's current value).
+__device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32_t tag) {
+  unsigned long long w = ld_tagged(p);
+  for (uint32_t i = 0; (uint32_t)(w >> 32) != tag; ++i) {
+    if (i > (1u << 24) || ((i & 1023u) == 1023u && error_set())) {
+      if (i > (1u << 24)) set_error(kDevTimeoutRed);
+      break;
+    }
+    w = ld_tagged(p);
+  }
+  return __uint_as_float((uint32_t)w);
+}
+// Four consecutive tagged words (two 16-byte loads), once all carry `tag`.
+__device__ __forceinline__ float4 wait_tagged4(const unsigned long long* p, uint32_t tag) {
+  ulonglong2 a = ld_tagged2(p), b = ld_tagged2(p + 2);
+  for (uint32_t i = 0; (uint32_t)(a.x >> 32) != tag || (uint32_t)(a.y >> 32) != tag || (uint32_t)(b.x >> 32) != tag ||
+                       (uint32_t)(b.y >> 32) != tag;
+       ++i) {
+    if (i > (1u << 24) || ((i & 1023u) == 1023u && error_set())) {
+      if (i > (1u << 24)) set_error(kDevTimeoutRed);
+      break;
+    }
+    a = ld_tagged2(p);
+    b = ld_tagged2(p + 2);
+  }
+  return make_float4(__uint_as_float((uint32_t)a.x), __uint_as_float((uint32_t)a.y), __uint_as_float((uint32_t)b.x),
+                     __uint_as_float((uint32_t)b.y));
 }
 // Consumers (256 threads) wait until `target` CTA-phase arrivals are counted.  One
 // thread polls (relaxed loads, then one acquire fence); the named barrier releases
 // the others.  Writers publish with bar.sync + one red.release (no full fence).
-// With ar_target > 0 (tensor parallelism, after an all-reduce phase) the thread also
-// waits until every source rank's counter in p.arrive reaches ar_target (each of the
-// G CTAs of every rank arrives once per all-reduce), then fences at system scope.
+// skip_grid (tensor parallelism, the phase after an all-reduce): the phase needs only
+// the all-reduced residual, whose words carry their own tags, so the consumers only
+// synchronise inside the CTA.
 template <int N>
-__device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid,
-                                          unsigned long long ar_target = 0) {
-  if (ctid == 0) {
+__device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid, bool skip_grid = false) {
+  if (ctid == 0 && !(N > 1 && skip_grid)) {
     uint32_t i = 0;
     while (ld_relaxed(p.bar) < target) {
       if (++i > (1u << 27) || ((i & 1023u) == 0 && error_set())) {
@@ -183,39 +219,16 @@ __device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, 
         break;
       }
     }
-    if (N > 1 && ar_target) {
-      for (int r = 0; r < N; ++r) {
-        uint32_t j = 0;
-        while (ld_relaxed_sys64(p.arrive + r) < ar_target) {
-          if (++j > (1u << 27) || ((j & 1023u) == 0 && error_set())) {
-            if (j > (1u << 27)) set_error(kDevTimeoutRed);
-            break;
-          }
-        }
-      }
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-    } else {
-      asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
   }
   named_bar_sync(1, kCW * 32);
 }
 // Arrival of this CTA for the current phase, by the warp that wrote its outputs.
-// peer: the warp stored partial rows into other ranks' memory.  The warp barrier
-// orders every lane's stores before lane 0's system-scope fence (cumulative, as the
-// CTA barrier + release of the local grid barrier); lane 0 then publishes to every
-// rank's counter for this source rank with relaxed reductions.
 template <int N>
-__device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, bool kv_written, bool peer = false) {
+__device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, bool kv_written) {
   if (kv_written) fence_proxy_async_global();   // KV rows (st.global) are read by TMA next phase
   __syncwarp();
-  if (lane == 0) {
-    red_release_add(p.bar, 1u);
-    if (N > 1 && peer) {
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      for (int r = 0; r < N; ++r) red_relaxed_sys_add64(p.peer_arrive[r] + p.rank, 1ull);
-    }
-  }
+  if (lane == 0) red_release_add(p.bar, 1u);
 }
 // Phase trace (globaltimer ns) for the first kTraceFrames steps when p.trace is set:
 // [cta][phase][0] = consumers released, [1] = consumers done, [2] = epilogue arrival,
@@ -294,8 +307,9 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 // buffer that receives h_old + sum of partials (written by CTA 0 only).
 struct ArIn {
   const float* h_old;
-  const float* recv;
+  const unsigned long long* recv;   // [N source][D] tagged words of this all-reduce's parity
   float* h_new;
+  uint32_t tag;
 };
 // WK consumer warps split the tile's K columns (chunk j of warp (wr, wk) is
 // column block wk + WK*j), the 8/WK row groups split its R rows.
@@ -323,7 +337,7 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
       v = __ldcg(reinterpret_cast<const float4*>(ar->h_old + col));
 #pragma unroll
       for (int r = 0; r < N; ++r) {
-        const float4 q = __ldcg(reinterpret_cast<const float4*>(ar->recv + r * D + col));
+        const float4 q = wait_tagged4(ar->recv + r * D + col, ar->tag);
         v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
       }
       if (c == 0) *reinterpret_cast<float4*>(ar->h_new + col) = v;
@@ -408,7 +422,8 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
 constexpr int kPeer = 100;
 template <int R, int EPI, int TG, int WK = kCW, int N = 1>
 __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t& rit, float* y, int rows, int T,
-                                         int off, int c, int G, int lane, int layer, int pos, int par = 0) {
+                                         int off, int c, int G, int lane, int layer, int pos,
+                                         unsigned long long ar_k = 0) {
   using TD = Tp<N>;
   constexpr int ORT = EPI == gemv::kSwiglu ? R / 2 : R;
   constexpr int RW = R / (kCW / WK);
@@ -437,7 +452,8 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
       const int row = t * R + r;
       if (live && row < rows)
 #pragma unroll
-        for (int q = 0; q < N; ++q) p.peer_recv[q][((long long)par * N + p.rank) * D + row] = val;
+        for (int q = 0; q < N; ++q)
+          st_tagged(p.peer_recv[q] + ((long long)(ar_k & 1) * N + p.rank) * D + row, val, (uint32_t)(ar_k + 1));
     } else if constexpr (EPI == gemv::kResid) {
       const int row = t * ORT + r;
       if (live && row < rows) y[row] = yold + val;
@@ -476,7 +492,7 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
       }
     }
   }
-  grid_arrive_warp<N>(p, lane, EPI == gemv::kQkv, EPI == kPeer);
+  grid_arrive_warp<N>(p, lane, EPI == gemv::kQkv);
   return true;
 }
 
@@ -835,14 +851,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         const int o2 = (int)((tiles_before + TD::TQKV + TD::TO) % G);
         const int o3 = (int)((tiles_before + TD::TQKV + TD::TO + TD::TW13) % G);
         const int kl = 1 + 5 * l;
-        const int par_o = (int)((kf + 2 * l) & 1), par_w2 = (int)((kf + 2 * l + 1) & 1);
+        const unsigned long long k_o = kf + 2 * l, k_w2 = kf + 2 * l + 1;
         if (!epilogue<6, gemv::kQkv, kTgQKV, kCW, N>(p, s, rit, nullptr, TD::QKVD, TD::TQKV, o0, c, G, lane, l, pos))
           return;
         trace_mark(p, c, f, kl, 2, L, lane);
         if constexpr (N == 1) {
           if (!epilogue<4, gemv::kResid, kTgO>(p, s, rit, p.h, D, TD::TO, o1, c, G, lane, l, pos)) return;
         } else {
-          if (!epilogue<TD::RO, kPeer, 1, TD::WKO, N>(p, s, rit, nullptr, D, TD::TO, o1, c, G, lane, l, pos, par_o))
+          if (!epilogue<TD::RO, kPeer, 1, TD::WKO, N>(p, s, rit, nullptr, D, TD::TO, o1, c, G, lane, l, pos, k_o))
             return;
         }
         trace_mark(p, c, f, kl + 2, 2, L, lane);
@@ -851,7 +867,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         if constexpr (N == 1) {
           if (!epilogue<2, gemv::kResid, kTgW2>(p, s, rit, p.h, D, TD::TW2, o3, c, G, lane, l, pos)) return;
         } else {
-          if (!epilogue<TD::RW2, kPeer, 1, TD::WKW2, N>(p, s, rit, nullptr, D, TD::TW2, o3, c, G, lane, l, pos, par_w2))
+          if (!epilogue<TD::RW2, kPeer, 1, TD::WKW2, N>(p, s, rit, nullptr, D, TD::TW2, o3, c, G, lane, l, pos, k_w2))
             return;
         }
         trace_mark(p, c, f, kl + 4, 2, L, lane);
@@ -876,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   // writes p.h and the last all-reduce of a launch leaves the residual in p.h.
   float* const hb[2] = {p.h, N > 1 ? p.h2 : p.h};
   auto ar_in = [&](unsigned long long k) {
-    return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1]};
+    return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1], (uint32_t)(k + 1)};
   };
   for (int f = 0; f < p.n_frames; ++f) {
     const int pos = pos0 + f, frame = frame0 + f;
@@ -933,7 +949,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       const unsigned long long k_o = kf + 2 * l, k_prev = kf + 2 * l - 1;   // k_prev: layer l-1's down
       // ---- QKV (+ RoPE + KV append in the epilogue warp); TP: h = all-reduce of layer l-1's down
       const bool ar_qkv = N > 1 && l > 0;
-      grid_wait<N>(p, phase * G, ctid, ar_qkv ? (k_prev + 1) * G : 0ull);
+      grid_wait<N>(p, phase * G, ctid, ar_qkv);
       trace_mark(p, c, f, kl, 0, L, ctid);
       const bool staged = prestage<N>(p, &kvmap, s, l, pos, c, ctid, a_pending);
       {
@@ -958,7 +974,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       trace_mark(p, c, f, kl + 2, 1, L, ctid);
       ++phase;
       // ---- gate/up + SwiGLU; TP: h = all-reduce of o_proj
-      grid_wait<N>(p, phase * G, ctid, N > 1 ? (k_o + 1) * G : 0ull);
+      grid_wait<N>(p, phase * G, ctid, true);
       trace_mark(p, c, f, kl + 3, 0, L, ctid);
       {
         const ArIn a = N > 1 ? ar_in(k_o) : ArIn{};
@@ -979,7 +995,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     // ---- FINAL norm (each CTA: full sum of squares, its slice of the output);
     // TP: h = all-reduce of the last layer's down (CTA 0 stores it to p.h)
     const unsigned long long k_last = kf + 2ull * L - 1;
-    grid_wait<N>(p, phase * G, ctid, N > 1 ? (k_last + 1) * G : 0ull);
+    grid_wait<N>(p, phase * G, ctid, true);
     trace_mark(p, c, f, 1 + 5 * L, 0, L, ctid);
     {
       const ArIn fa = N > 1 ? ar_in(k_last) : ArIn{};
@@ -987,7 +1003,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         if (N == 1) return p.h[i];
         float v = __ldcg(fa.h_old + i);
 #pragma unroll
-        for (int r = 0; r < N; ++r) v += __ldcg(fa.recv + r * D + i);
+        for (int r = 0; r < N; ++r) v += wait_tagged(fa.recv + r * D + i, fa.tag);
         return v;
       };
       float ss = 0.f;

@@ -145,8 +145,8 @@ struct vx_handle {
 
   // TP
   ncclComm_t comm = nullptr;
-  // TP persistent kernel: receive buffers + arrival counters in peer-accessible memory
-  // (CUDA IPC), the residual's second buffer, and all-reduces completed so far
+  // TP persistent kernel: tagged receive words in peer-accessible memory (CUDA IPC),
+  // the residual's second buffer, and all-reduces completed so far
   void* p2p_buf = nullptr;
   void* p2p_peer[mk::kMaxTp] = {nullptr};
   bool p2p_ready = false;
@@ -256,10 +256,9 @@ int prime_kernel_attrs(vx_handle* h) {
 
 // n_frames consecutive backbone steps of one slot in ONE cooperative launch of the
 // persistent decode kernel (k_step.cuh).
-// Peer-accessible block of the TP persistent kernel: receive buffers [2][tp][D]
-// floats, then one 64-bit arrival counter per source rank.
-constexpr size_t kP2pCounterOff = 256 * 1024;
-constexpr size_t kP2pBytes = kP2pCounterOff + 4096;
+// Peer-accessible block of the TP persistent kernel: tagged receive words
+// [2 parity][tp source][D] (8 bytes each; zero = no tag yet).
+constexpr size_t kP2pBytes = 2ull * mk::kMaxTp * 3072 * 8;
 
 int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, int mode_next, bool inc_frame,
                  bool record) {
@@ -299,12 +298,8 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
     if (!h->p2p_ready) return h->fail(VX_E_STATE, "tensor-parallel persistent kernel needs vx_tp_p2p_open");
     sp.rank = h->rank;
     sp.h2 = h->h2 + slot * D;
-    sp.recv = reinterpret_cast<float*>(h->p2p_buf);
-    sp.arrive = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(h->p2p_buf) + kP2pCounterOff);
-    for (int r = 0; r < h->tp; ++r) {
-      sp.peer_recv[r] = reinterpret_cast<float*>(h->p2p_peer[r]);
-      sp.peer_arrive[r] = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(h->p2p_peer[r]) + kP2pCounterOff);
-    }
+    sp.recv = reinterpret_cast<unsigned long long*>(h->p2p_buf);
+    for (int r = 0; r < h->tp; ++r) sp.peer_recv[r] = reinterpret_cast<unsigned long long*>(h->p2p_peer[r]);
     sp.ar_base = h->ar_base;
   }
   h->launches++;
@@ -1773,7 +1768,7 @@ int vx_tp_p2p_handle(vx_handle* h, uint8_t out[64]) {
   CK(cudaSetDevice(h->dev));
   if (!h->p2p_buf) {
     CK(cudaMalloc(&h->p2p_buf, kP2pBytes));
-    CK(cudaMemset(h->p2p_buf, 0, kP2pBytes));   // arrival counters start at zero on every rank
+    CK(cudaMemset(h->p2p_buf, 0, kP2pBytes));   // tag 0 never matches an all-reduce (tags start at 1)
     CK(cudaDeviceSynchronize());
   }
   cudaIpcMemHandle_t mh;
