@@ -454,7 +454,9 @@ def run_b200(args):
                        "parallelism": f"dp{world}" if tp == 1 else f"tp{tp}",
                        "l2": "inputs larger than L2: 6.05 GB of weights streamed per frame"},
             "roofline": {"bound": "hbm", "kernel": "k_decode_steps (persistent decode kernel, one launch per step)"
-                                                    if tp == 1 else "per-op kernels + NCCL (TP)",
+                                                    if tp == 1 else
+                                                    f"k_decode_steps<{tp}> (persistent decode kernel per rank, "
+                                                    "all-reduces over peer memory inside the kernel)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes_per_launch": launch_bytes,
                          "launch_ms": ms_per_step,

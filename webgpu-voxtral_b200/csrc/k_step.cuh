@@ -107,6 +107,7 @@ struct StepParams {
   float* h2;                          // second residual buffer (h alternates per all-reduce)
   unsigned long long* recv;           // this rank's receive words [2 parity][N source][D]: tag << 32 | f32 bits
   unsigned long long* peer_recv[kMaxTp];   // every rank's receive words (index = rank; own one included)
+  unsigned long long* hx;             // local tagged words of the summed residual [2 parity][D]
   unsigned long long ar_base;         // all-reduces completed before this launch
 };
 
@@ -174,8 +175,7 @@ __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long
   asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Value of a tagged word once its tag is `tag` (bounded poll: an expired wait records
-// an error and returns the word's current value).
+// Value of a tagged word once its tag is `tag` (bounded poll, as below).
 __device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32_t tag) {
   unsigned long long w = ld_tagged(p);
   for (uint32_t i = 0; (uint32_t)(w >> 32) != tag; ++i) {
@@ -187,7 +187,8 @@ __device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32
   }
   return __uint_as_float((uint32_t)w);
 }
-// Four consecutive tagged words (two 16-byte loads), once all carry `tag`.
+// Four consecutive tagged words (two 16-byte loads), once all carry `tag` (bounded
+// poll: an expired wait records an error and returns the words' current values).
 __device__ __forceinline__ float4 wait_tagged4(const unsigned long long* p, uint32_t tag) {
   ulonglong2 a = ld_tagged2(p), b = ld_tagged2(p + 2);
   for (uint32_t i = 0; (uint32_t)(a.x >> 32) != tag || (uint32_t)(a.y >> 32) != tag || (uint32_t)(b.x >> 32) != tag ||
@@ -302,15 +303,87 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 // Tiles are consumed in groups of TG: each ring stage is released right after its
 // FMAs, but the cross-lane reduction, the reduction-slot handoff and the epilogue run
 // once per group (TG*R <= 32 outputs), which amortises their latency over TG tiles.
-// Inputs of a phase that follows a tensor-parallel all-reduce: the residual before
-// it (h_old), this rank's receive buffer of the all-reduce ([N source][D]) and the
-// buffer that receives h_old + sum of partials (written by CTA 0 only).
+// Inputs of a phase that follows a tensor-parallel all-reduce.  At N = 8 the
+// reduction runs in two stages inside the rank: (A) CTA c sums its slice [e0, e1) of
+// the row over the N sources (h_old + partials in rank order), stores it to h_new and
+// publishes it as tagged words in hx; (B) every CTA reads the whole summed row from
+// hx.  A CTA only ever reads back its own slice of h_old / h_new, so those need no
+// synchronisation.  At N <= 4 every CTA sums the whole row itself (ar_sum4) and CTA 0
+// stores it to h_new.
 struct ArIn {
   const float* h_old;
   const unsigned long long* recv;   // [N source][D] tagged words of this all-reduce's parity
   float* h_new;
   uint32_t tag;
+  unsigned long long* hx;           // [D] tagged words of the summed row (this parity)
+  int e0, e1;
 };
+__device__ __forceinline__ bool tags_are(const ulonglong2& a, const ulonglong2& b, uint32_t tag) {
+  return (uint32_t)(a.x >> 32) == tag && (uint32_t)(a.y >> 32) == tag && (uint32_t)(b.x >> 32) == tag &&
+         (uint32_t)(b.y >> 32) == tag;
+}
+// One-stage form (N <= 4): h_old + sum over source ranks 0..N-1 (in that order) of 4
+// consecutive columns, read by every CTA for the whole row.  The loads of up to 4
+// sources are issued before any tag is checked.
+template <int N>
+__device__ __forceinline__ float4 ar_sum4(const ArIn& a, int col) {
+  constexpr int GS = N < 4 ? N : 4;
+  float4 v = __ldcg(reinterpret_cast<const float4*>(a.h_old + col));
+#pragma unroll
+  for (int r0 = 0; r0 < N; r0 += GS) {
+    ulonglong2 w[GS][2];
+#pragma unroll
+    for (int g = 0; g < GS; ++g) {
+      const unsigned long long* q = a.recv + (long long)(r0 + g) * D + col;
+      w[g][0] = ld_tagged2(q);
+      w[g][1] = ld_tagged2(q + 2);
+    }
+#pragma unroll
+    for (int g = 0; g < GS; ++g) {
+      const float4 x = tags_are(w[g][0], w[g][1], a.tag)
+                           ? make_float4(__uint_as_float((uint32_t)w[g][0].x), __uint_as_float((uint32_t)w[g][0].y),
+                                         __uint_as_float((uint32_t)w[g][1].x), __uint_as_float((uint32_t)w[g][1].y))
+                           : wait_tagged4(a.recv + (long long)(r0 + g) * D + col, a.tag);
+      v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+    }
+  }
+  return v;
+}
+// Two stages for N = 8, where every CTA reading all N x D words is the cost.
+template <int N>
+constexpr bool kArTwoStage = N >= 8;
+// Stage A for thread t of the CTA's consumers: element e0 + t of the slice (the N
+// source loads are issued before any tag is checked).
+template <int N>
+__device__ __forceinline__ void ar_stage_a(const ArIn& a, int t) {
+  for (int i = a.e0 + t; i < a.e1; i += kCW * 32) {
+    float v = __ldcg(a.h_old + i);
+    unsigned long long w[N];
+#pragma unroll
+    for (int r = 0; r < N; ++r) w[r] = ld_tagged(a.recv + (long long)r * D + i);
+#pragma unroll
+    for (int r = 0; r < N; ++r)
+      v += (uint32_t)(w[r] >> 32) == a.tag ? __uint_as_float((uint32_t)w[r]) : wait_tagged(a.recv + (long long)r * D + i, a.tag);
+    a.h_new[i] = v;
+    st_tagged(a.hx + i, v, a.tag);
+  }
+}
+// Stage B: CPL groups of 4 summed columns (all loads issued before the tag checks).
+template <int CPL>
+__device__ __forceinline__ void ar_stage_b(const ArIn& a, const int (&col)[CPL], float4 (&v)[CPL]) {
+  ulonglong2 w[CPL][2];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    w[j][0] = ld_tagged2(a.hx + col[j]);
+    w[j][1] = ld_tagged2(a.hx + col[j] + 2);
+  }
+#pragma unroll
+  for (int j = 0; j < CPL; ++j)
+    v[j] = tags_are(w[j][0], w[j][1], a.tag)
+               ? make_float4(__uint_as_float((uint32_t)w[j][0].x), __uint_as_float((uint32_t)w[j][0].y),
+                             __uint_as_float((uint32_t)w[j][1].x), __uint_as_float((uint32_t)w[j][1].y))
+               : wait_tagged4(a.hx + col[j], a.tag);
+}
 // WK consumer warps split the tile's K columns (chunk j of warp (wr, wk) is
 // column block wk + WK*j), the 8/WK row groups split its R rows.
 template <int R, int CPL, bool NORM, int TG, int WK = kCW, int N = 1>
@@ -328,19 +401,29 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
   float xr[CPL][4];
   float2 wn[CPL][2];
   float ss = 0.f;
+  float4 hv[CPL];
+  if (N > 1 && ar) {
+    // all-reduce: h = h_old + partials of ranks 0..N-1, the same order on every rank
+    int cols[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) cols[j] = (wk + WK * j) * 128 + lane * 4;
+    if constexpr (kArTwoStage<N>) {
+      ar_stage_a<N>(*ar, cw * 32 + lane);
+      ar_stage_b<CPL>(*ar, cols, hv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        hv[j] = ar_sum4<N>(*ar, cols[j]);
+        if (c == 0) *reinterpret_cast<float4*>(ar->h_new + cols[j]) = hv[j];
+      }
+    }
+  }
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
     const int col = (wk + WK * j) * 128 + lane * 4;
     float4 v;
     if (N > 1 && ar) {
-      // all-reduce: h = h_old + partials of ranks 0..N-1, the same order on every rank
-      v = __ldcg(reinterpret_cast<const float4*>(ar->h_old + col));
-#pragma unroll
-      for (int r = 0; r < N; ++r) {
-        const float4 q = wait_tagged4(ar->recv + r * D + col, ar->tag);
-        v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
-      }
-      if (c == 0) *reinterpret_cast<float4*>(ar->h_new + col) = v;
+      v = hv[j];
     } else {
       v = *reinterpret_cast<const float4*>(x + col);
     }
@@ -892,7 +975,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   // writes p.h and the last all-reduce of a launch leaves the residual in p.h.
   float* const hb[2] = {p.h, N > 1 ? p.h2 : p.h};
   auto ar_in = [&](unsigned long long k) {
-    return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1], (uint32_t)(k + 1)};
+    return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1], (uint32_t)(k + 1),
+                p.hx + (long long)(k & 1) * D, e0, e1};
   };
   for (int f = 0; f < p.n_frames; ++f) {
     const int pos = pos0 + f, frame = frame0 + f;
@@ -999,18 +1083,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     trace_mark(p, c, f, 1 + 5 * L, 0, L, ctid);
     {
       const ArIn fa = N > 1 ? ar_in(k_last) : ArIn{};
-      auto hval = [&](int i) -> float {
-        if (N == 1) return p.h[i];
-        float v = __ldcg(fa.h_old + i);
-#pragma unroll
-        for (int r = 0; r < N; ++r) v += wait_tagged(fa.recv + r * D + i, fa.tag);
-        return v;
-      };
+      // TP, two stages: stage A leaves this CTA's slice in fa.h_new (= p.h), written by
+      // the same threads that read it back in the slice pass below.  One stage: the
+      // summed row is staged in the (idle) attention buffer for the slice pass.
+      float* hs = reinterpret_cast<float*>(s.attn);
+      auto hval = [&](int i) -> float { return N == 1 ? p.h[i] : kArTwoStage<N> ? fa.h_new[i] : hs[i]; };
       float ss = 0.f;
-      for (int i = ctid; i < D; i += kCW * 32) {
-        const float v = hval(i);
-        ss += v * v;
-        if (N > 1 && c == 0) fa.h_new[i] = v;
+      if constexpr (N == 1) {
+        for (int i = ctid; i < D; i += kCW * 32) ss += p.h[i] * p.h[i];
+      } else {
+        constexpr int U = D / (kCW * 32 * 4);
+        int cols[U];
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) cols[u] = (ctid + kCW * 32 * u) * 4;
+        if constexpr (kArTwoStage<N>) {
+          ar_stage_a<N>(fa, ctid);
+          ar_stage_b<U>(fa, cols, v);
+        } else {
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            v[u] = ar_sum4<N>(fa, cols[u]);
+            *reinterpret_cast<float4*>(hs + cols[u]) = v[u];
+            if (c == 0) *reinterpret_cast<float4*>(fa.h_new + cols[u]) = v[u];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
       }
       ss = warp_sum(ss);
       if (lane == 0) s.scratch[cw] = ss;

@@ -257,8 +257,10 @@ int prime_kernel_attrs(vx_handle* h) {
 // n_frames consecutive backbone steps of one slot in ONE cooperative launch of the
 // persistent decode kernel (k_step.cuh).
 // Peer-accessible block of the TP persistent kernel: tagged receive words
-// [2 parity][tp source][D] (8 bytes each; zero = no tag yet).
-constexpr size_t kP2pBytes = 2ull * mk::kMaxTp * 3072 * 8;
+// [2 parity][tp source][D] (8 bytes each; zero = no tag yet), then this rank's own
+// tagged words of the summed residual [2 parity][D] (read only locally).
+constexpr size_t kP2pHxOff = 2ull * mk::kMaxTp * 3072 * 8;
+constexpr size_t kP2pBytes = kP2pHxOff + 2ull * 3072 * 8;
 
 int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, int mode_next, bool inc_frame,
                  bool record) {
@@ -300,6 +302,7 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
     sp.h2 = h->h2 + slot * D;
     sp.recv = reinterpret_cast<unsigned long long*>(h->p2p_buf);
     for (int r = 0; r < h->tp; ++r) sp.peer_recv[r] = reinterpret_cast<unsigned long long*>(h->p2p_peer[r]);
+    sp.hx = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(h->p2p_buf) + kP2pHxOff);
     sp.ar_base = h->ar_base;
   }
   h->launches++;
