@@ -159,8 +159,8 @@ struct vx_handle {
   mk::LayerPtrs* d_layers = nullptr;
   unsigned* d_bar = nullptr;
   unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
-  int prefetch_ahead = 8;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD)
-  int prestage_kv = 1;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV)
+  int prefetch_ahead = 4;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD; measured best)
+  int prestage_kv = 0;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV=1; measured slower)
   bool trace_armed = false;
 
   // token batches on the tensor cores (k_gemm.cuh): batched prefill
