@@ -86,6 +86,18 @@ int vx_init_random_weights(vx_handle* h, uint64_t seed);
  * unknown name or a wrong element count. */
 int vx_load_tensor(vx_handle* h, const char* name, const uint16_t* f16, size_t n_elems);
 
+/* The checkpoint tensor names the engine holds (the keys organizeWeights expects,
+ * src/engine.ts:659-743), sorted and newline-separated into buf (NUL-terminated, cut at
+ * len).  Returns the bytes needed, terminator included. */
+size_t vx_tensor_names(const vx_handle* h, char* buf, size_t len);
+
+/* One checkpoint tensor in its stored dtype (0 F16, 1 BF16, 2 F32, little endian, full
+ * tensor as in vx_load_tensor), converted to F16 on the GPU with the reference loader's
+ * bit rules: convertBF16toF16 (src/weights.ts:94-138) and float32ToFloat16
+ * (src/weights.ts:222-232).  The first call allocates a 64 MB staging buffer.  Replaces
+ * loadTensorFromSafetensors / loadFromSafetensors (src/weights.ts:182-215, :491-669). */
+int vx_load_tensor_typed(vx_handle* h, const char* name, const void* data, int32_t dtype, size_t n_elems);
+
 /* Completion of loadWeights() after the vx_load_tensor calls: builds the derived
  * frame-independent tables (time_projection of the 7 Euler times). */
 int vx_mark_weights_loaded(vx_handle* h);

@@ -112,6 +112,53 @@ __global__ void k_fill_kv_slot(const __grid_constant__ FillKvParams p) {
   }
 }
 
+// ------------------------------------------------------------------ checkpoint conversion
+// Checkpoint tensors arrive as BF16 (the published checkpoint) or F32 and are stored
+// as F16 with the reference loader's bit rules (src/weights.ts), so that both
+// implementations hold identical weights:
+//   BF16 -> F16 (convertBF16toF16, :94-138): sign kept; BF16 zero / subnormal -> signed
+//   zero; Inf / NaN kept (NaN quieted to mantissa 0x200); exponent above F16 range ->
+//   Inf; below -> F16 subnormal by right shift (truncating), or zero; else the 7-bit
+//   mantissa extended with three zero bits.
+//   F32 -> F16 (float32ToFloat16, :222-232): truncating; exponent <= 0 after rebias ->
+//   signed zero (no subnormals); >= 31 -> Inf (NaN included).
+__device__ __forceinline__ uint16_t bf16_bits_to_f16_bits(uint16_t b) {
+  const uint16_t sign = (uint16_t)(b & 0x8000u);
+  const int exp = (b >> 7) & 0xFF;
+  const int mant = b & 0x7F;
+  if (exp == 0xFF) return (uint16_t)(sign | 0x7C00u | (mant ? 0x0200u : 0u));
+  if (exp == 0) return sign;
+  const int unbiased = exp - 127;
+  if (unbiased > 15) return (uint16_t)(sign | 0x7C00u);
+  if (unbiased < -14) {
+    const int shift = -14 - unbiased;
+    if (shift > 10) return sign;
+    return (uint16_t)(sign | ((((0x80 | (mant << 1)) >> shift) >> 1) & 0x03FF));
+  }
+  return (uint16_t)(sign | ((unbiased + 15) << 10) | ((mant << 3) & 0x03FF));
+}
+__device__ __forceinline__ uint16_t f32_bits_to_f16_bits(uint32_t b) {
+  const uint16_t sign = (uint16_t)((b >> 16) & 0x8000u);
+  const int exp = (int)((b >> 23) & 0xFF) - 127 + 15;
+  const uint16_t frac = (uint16_t)((b >> 13) & 0x3FF);
+  if (exp <= 0) return sign;
+  if (exp >= 31) return (uint16_t)(sign | 0x7C00u);
+  return (uint16_t)(sign | (exp << 10) | frac);
+}
+// src [rows][cols] (dtype 0 F16, 1 BF16, 2 F32, packed) -> dst [rows] with row stride ld.
+__global__ void k_convert_to_f16(const void* __restrict__ src, int dtype, long long rows, long long cols,
+                                 uint16_t* __restrict__ dst, long long ld) {
+  const long long n = rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cols, c = i % cols;
+    uint16_t v;
+    if (dtype == 1) v = bf16_bits_to_f16_bits(static_cast<const uint16_t*>(src)[i]);
+    else if (dtype == 2) v = f32_bits_to_f16_bits(static_cast<const uint32_t*>(src)[i]);
+    else v = static_cast<const uint16_t*>(src)[i];
+    dst[r * ld + c] = v;
+  }
+}
+
 // ------------------------------------------------------------------ embedding
 struct EmbedParams {
   const __half* tok;   int vocab;

@@ -141,6 +141,7 @@ struct vx_handle {
 
   // staging
   uint8_t* pinned = nullptr;
+  void* load_stage = nullptr;   // vx_load_tensor_typed staging (allocated by the first call)
   size_t pinned_bytes = 0;
 
   // TP
@@ -1177,6 +1178,7 @@ void vx_destroy(vx_handle* h) {
   if (h->d_trace) cudaFree(h->d_trace);
   if (h->kv_pool) cudaFree(h->kv_pool);
   if (h->tb_buf) cudaFree(h->tb_buf);
+  if (h->load_stage) cudaFree(h->load_stage);
   if (h->rope_freq) cudaFree(h->rope_freq);   // base of the activation block
   if (h->pinned) cudaFreeHost(h->pinned);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
@@ -1283,6 +1285,47 @@ int vx_init_random_weights(vx_handle* h, uint64_t seed) {
   h->weights_ready = true;
   if (h->cfg.enable_fm) return build_tp_table(h);
   return VX_OK;
+}
+
+int vx_load_tensor_typed(vx_handle* h, const char* name, const void* data, int32_t dtype, size_t n) {
+  if (!h || !name || !data) return VX_E_INVALID;
+  if (dtype < 0 || dtype > 2) return h->fail(VX_E_INVALID, "dtype %d (0 F16, 1 BF16, 2 F32)", dtype);
+  auto it = h->tensors.find(name);
+  if (it == h->tensors.end()) return h->fail(VX_E_INVALID, "Missing weight: %s", name);
+  const TensorSlot& t = it->second;
+  if ((long long)n != t.full_rows * t.full_cols)
+    return h->fail(VX_E_INVALID, "%s: expected %lld elements, got %zu", name, t.full_rows * t.full_cols, n);
+  CK(cudaSetDevice(h->dev));
+  const size_t es = dtype == 2 ? 4 : 2;
+  // The rank's block goes through a bounded device staging buffer, a chunk of rows at a time.
+  constexpr size_t kStage = 64ull << 20;
+  if (!h->load_stage) CK(cudaMalloc(&h->load_stage, kStage));
+  const long long rows_per = std::max<long long>(1, (long long)(kStage / (t.cols * es)));
+  const uint8_t* base = static_cast<const uint8_t*>(data) + ((size_t)t.row0 * t.full_cols + t.col0) * es;
+  for (long long r0 = 0; r0 < t.rows; r0 += rows_per) {
+    const long long nr = std::min(rows_per, t.rows - r0);
+    CK(cudaMemcpy2DAsync(h->load_stage, t.cols * es, base + (size_t)r0 * t.full_cols * es, t.full_cols * es,
+                         t.cols * es, nr, cudaMemcpyHostToDevice, h->stream));
+    const long long cnt = nr * t.cols;
+    CK(launch(h, k_convert_to_f16, dim3((unsigned)std::min<long long>((cnt + 255) / 256, 16L * h->num_sms)), dim3(256),
+              0, (const void*)h->load_stage, dtype, nr, t.cols, reinterpret_cast<uint16_t*>(t.dst + r0 * t.ld), t.ld));
+  }
+  return finish(h);
+}
+
+size_t vx_tensor_names(const vx_handle* h, char* buf, size_t len) {
+  if (!h) return 0;
+  std::vector<std::string> names;
+  for (const auto& kv : h->tensors) names.push_back(kv.first);
+  std::sort(names.begin(), names.end());
+  std::string all;
+  for (const auto& n : names) { all += n; all += '\n'; }
+  if (buf && len) {
+    const size_t k = std::min(len - 1, all.size());
+    memcpy(buf, all.data(), k);
+    buf[k] = 0;
+  }
+  return all.size() + 1;
 }
 
 size_t vx_tensor_numel(const vx_handle* h, const char* name) {

@@ -79,6 +79,8 @@ def load_library():
         "vx_last_error": (ctypes.c_char_p, [H]),
         "vx_init_random_weights": (ctypes.c_int, [H, ctypes.c_uint64]),
         "vx_load_tensor": (ctypes.c_int, [H, ctypes.c_char_p, _u16p, ctypes.c_size_t]),
+        "vx_load_tensor_typed": (ctypes.c_int, [H, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t]),
+        "vx_tensor_names": (ctypes.c_size_t, [H, ctypes.c_char_p, ctypes.c_size_t]),
         "vx_tensor_numel": (ctypes.c_size_t, [H, ctypes.c_char_p]),
         "vx_read_tensor": (ctypes.c_int, [H, ctypes.c_char_p, _u16p, ctypes.c_size_t]),
         "vx_mark_weights_loaded": (ctypes.c_int, [H]),
@@ -209,6 +211,48 @@ class VoxtralEngine:
             self._check(L.vx_load_tensor(self._h, name.encode(), _p(a, _u16p), a.size))
         self._check(L.vx_mark_weights_loaded(self._h))
         self._ready = True
+
+    def tensorNames(self) -> list:
+        """Checkpoint tensor names this engine holds (sorted)."""
+        L = load_library()
+        n = L.vx_tensor_names(self._h, None, 0)
+        buf = ctypes.create_string_buffer(n)
+        L.vx_tensor_names(self._h, buf, n)
+        return [x for x in buf.value.decode().split("\n") if x]
+
+    def loadWeightsFromSafetensors(self, path: str, required: bool = True) -> list:
+        """loadWeightsFromHF / loadFromSafetensors (src/engine.ts:569, src/weights.ts:491-669)
+        from a local safetensors file: every tensor the engine has a slot for is copied in its
+        stored dtype and converted to F16 on the GPU (BF16 and F32 with the reference's bit
+        rules).  Tensors the engine does not use (codec, tokenizer extras) are skipped.  With
+        `required`, a slot the file does not provide raises, as the reference throws
+        "Missing weight".  Returns the loaded names."""
+        from .safetensors import DTYPES, SafetensorsFile
+        L = load_library()
+        st = SafetensorsFile(path)
+        loaded = []
+        try:
+            for name in st.names():
+                n = L.vx_tensor_numel(self._h, name.encode())
+                if n == 0:
+                    continue
+                raw, dt = st.raw(name)
+                code = DTYPES[dt][1]
+                if code is None:
+                    raise VoxtralError(-1, f"{name}: dtype {dt} cannot be loaded as a weight")
+                self._check(L.vx_load_tensor_typed(self._h, name.encode(), raw.ctypes.data_as(ctypes.c_void_p),
+                                                   code, raw.size))
+                loaded.append(name)
+                del raw
+        finally:
+            st.close()
+        if required:
+            missing = [m for m in self.tensorNames() if m not in set(loaded)]
+            if missing:
+                raise VoxtralError(-1, f"Missing weight: {missing[0]} (and {len(missing) - 1} more)")
+        self._check(L.vx_mark_weights_loaded(self._h))
+        self._ready = True
+        return loaded
 
     def readTensor(self, name: str) -> np.ndarray:
         L = load_library()
