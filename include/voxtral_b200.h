@@ -180,6 +180,15 @@ int vx_fill_kv(vx_handle* h, int32_t slot, int32_t n_positions, uint64_t seed);
  * `utt` selects the utterance stream of vx_rng.h. */
 int vx_set_streams(vx_handle* h, int32_t slot, uint64_t noise_seed, uint64_t codes_seed, int32_t utt);
 
+/* Semantic code selection of the slot's FM frames.  mode 0 (default): masked argmax
+ * (index 0 and >= 8194 masked, ties to the lowest index).  mode 1: the reference's
+ * temperature + top-p sampling, sampleTopP(semLogits, 0.9, 0.8) of generate()
+ * (src/engine.ts:247-289, called at :2565 on the logits masked at :2559-2563), run on
+ * the device inside the FM graph; the uniform draw of frame f is counter f of the
+ * stream (seed, "sample") of vx_rng.h in place of Math.random.  Every TP rank must
+ * be given the same seed. */
+int vx_set_sampling(vx_handle* h, int32_t slot, int32_t mode, double top_p, double temperature, uint64_t seed);
+
 /* Codes of frames [frame0, frame0+n): out [n][37] = semantic, 36 acoustic. */
 int vx_read_codes(vx_handle* h, int32_t slot, int32_t frame0, int32_t n, uint32_t* out);
 /* Final-norm state of frames [frame0, frame0+n): out [n][dim]. */
@@ -226,6 +235,12 @@ int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t*
  * out_rel_err[2] = max|Y - Yref| / max|Yref| of the two passes. */
 int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, int32_t max_splits, uint64_t seed,
                      double* out_rel_err);
+
+/* Test support for the device top-p sampler (sampleTopP, src/engine.ts:247-289): the
+ * logits[n] (n <= 16384) with indices outside [valid_lo, valid_hi) masked to -Inf, one
+ * sample per uniform draw u[i] in [0, 1) (the reference's Math.random()), out[i] = index. */
+int vx_selftest_top_p(vx_handle* h, const float* logits, int32_t n, int32_t valid_lo, int32_t valid_hi, double top_p,
+                      double temperature, const double* u, int32_t n_draws, int32_t* out);
 
 /* Tensor parallelism over NCCL (batch-1 latency, heads and FFN columns
  * sharded): the unique id comes from vx_nccl_unique_id on rank 0 and is shared by

@@ -8,8 +8,8 @@ importlib:
     vx = importlib.import_module("webgpu-voxtral_b200")
 """
 from .engine import (TTSResult, VoxtralEngine, VoxtralError, default_config, header_symbols, library_path,
-                     load_library, nccl_unique_id, sample_top_p, tp_init)
+                     load_library, nccl_unique_id, tp_init)
 from . import synth
 
 __all__ = ["VoxtralEngine", "VoxtralError", "TTSResult", "default_config", "header_symbols", "library_path",
-           "load_library", "nccl_unique_id", "tp_init", "sample_top_p", "synth"]
+           "load_library", "nccl_unique_id", "tp_init", "synth"]

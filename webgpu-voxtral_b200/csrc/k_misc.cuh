@@ -23,6 +23,10 @@ struct SlotState {
   uint64_t noise_key;   // FM noise stream
   int32_t noise_mode;   // 0: FM noise from noise_key, 1: from the host-written noise row
   int32_t max_frames;   // capacity of the code ring
+  int32_t sample_mode;  // semantic code: 0 masked argmax, 1 temperature + top-p sampling
+  int32_t sample_pad;
+  double top_p, temperature;   // sampling parameters (doubles, as the reference's JS numbers)
+  uint64_t sample_key;  // stream of the sampler's uniform draws (counter = frame)
 };
 static_assert(sizeof(SlotState) % 8 == 0, "SlotState layout");
 constexpr int kPosStride = sizeof(SlotState) / 4;
@@ -47,6 +51,9 @@ struct SlotUpdate {
   int32_t set_keys;
   uint64_t codes_key, noise_key;
   int32_t set_prompt_len, prompt_len;
+  int32_t set_sampling, sample_mode;
+  double top_p, temperature;
+  uint64_t sample_key;
 };
 __global__ void k_slot_update(SlotState* slots, int slot, SlotUpdate u) {
   SlotState& s = slots[slot];
@@ -57,6 +64,12 @@ __global__ void k_slot_update(SlotState* slots, int slot, SlotUpdate u) {
   if (u.set_counters) { s.pos = u.pos; s.frame = u.frame; }
   if (u.set_keys) { s.codes_key = u.codes_key; s.noise_key = u.noise_key; }
   if (u.set_prompt_len) s.prompt_len = u.prompt_len;
+  if (u.set_sampling) {
+    s.sample_mode = u.sample_mode;
+    s.top_p = u.top_p;
+    s.temperature = u.temperature;
+    s.sample_key = u.sample_key;
+  }
 }
 
 constexpr int kSemValid = 8194;     // 8192 semantic codes + 2 specials (src/engine.ts:2559-2563)
@@ -395,6 +408,412 @@ __global__ void __launch_bounds__(1024) k_fm_prepare(const __grid_constant__ FmP
     p.x[threadIdx.x] = st.noise_mode ? p.host_noise[threadIdx.x]
                                      : vx_normal(st.noise_key, (uint64_t)st.frame * kNumAc + threadIdx.x);
   }
+}
+
+// ------------------------------------------------------------------ top-p sampling
+// sampleTopP (src/engine.ts:247-289) over the masked semantic logits (indices outside
+// [valid_lo, valid_hi) are -Inf, :2559-2563), in one CTA of 1024 threads:
+//   scaled = f32(logit / temperature) and probabilities f32(exp(f64(scaled) - max) /
+//   sum), with the exponentials and their sum in f64 as the reference computes them.
+// The reference then sorts by descending probability (stable: ties in index order),
+// cuts at the first position whose running sum reaches top_p, and walks the kept
+// prefix to the first position whose running sum reaches u * (sum of the kept).
+// Here no full sort is made.  Running sums are carried in 2^-63 fixed point (64-bit
+// integers, so every order of addition gives the same value).  The row is grouped by
+// the first 12 bits of the key 0x7FFFFFFF - (probability bits) (a counting sort; the
+// key ascends in the reference's order); the group in which the running sum reaches
+// a target is found from the prefix sums of the grouped row, and only that group is
+// put in exact order (pairwise ranking of (key, index); a group of more than 1024 is
+// regrouped by two more digits of the key the same way, down to one run of equal
+// probabilities, inside which the order is the index order).  The fixed-point sums differ from the reference's
+// sequential f64 sums by < 1e-12, which changes the result only when a running sum
+// lies that close to its threshold.
+constexpr int kSortN = 16384;                 // largest row (>= semantic vocabulary)
+constexpr int kTpPer = kSortN / 1024;         // thread t holds positions [t*kTpPer, (t+1)*kTpPer)
+constexpr int kTpDigits = 4096;               // first digit: key bits 30..19
+constexpr int kTpRankMax = 1024;              // largest group ordered by pairwise ranking
+constexpr uint32_t kTpNone = 0xFFFFFFFFu;     // key of a position past the row
+struct TopPSmem {
+  uint32_t key[kSortN];                       // exponentials (f32 bits) first, then keys
+  unsigned long long pk[kTpRankMax];          // the group being ranked: key << 16 | index
+  uint16_t by_digit[kSortN];                  // row indices grouped by first digit
+  uint16_t deep[kSortN];                      // a large group regrouped by its second digit
+  uint16_t order[kSortN];                     // the ranked group in exact order / third-digit regrouping
+  uint32_t cnt[kTpDigits];                    // first-digit counts, then fill counters
+  uint32_t off[kTpDigits + 1];                // start of each digit in by_digit
+  uint32_t sub_cnt[1024];
+  uint32_t sub_off[1024];
+};
+constexpr size_t kSampleSmem = sizeof(TopPSmem);
+constexpr uint64_t kSampleStream = 0x73616d706c65ull;   // stream id of the sampler's draws ("sample")
+
+// Fixed-point (2^-63) value of the probability whose key is k, floor(p * 2^63), from
+// the f32 fields: p = M * 2^(E - 150) (M with its hidden bit), so p * 2^63 = M << (E - 87).
+__device__ __forceinline__ unsigned long long tp_fixed(uint32_t k) {
+  const uint32_t b = 0x7FFFFFFFu - k;
+  const int e = (int)(b >> 23);
+  const unsigned long long m = (b & 0x7FFFFFu) | (e ? 0x800000u : 0u);
+  const int sh = (e ? e : 1) - 87;
+  return sh >= 0 ? (m << sh) : (sh > -64 ? (m >> -sh) : 0ull);
+}
+
+// f32(a / t) given r = f64(1 / t): a * r lies within 3 f64 ulps of the f64 quotient,
+// so rounding it to f32 gives the same result unless it lies within a few f64 ulps of
+// a tie between two f32 values (the 29 bits that f32 rounding drops are near
+// 0x10000000) or outside the f32 normal range; those take the division.
+__device__ __forceinline__ float tp_div_f32(double a, double r, double t) {
+  const double d = a * r;
+  const unsigned long long b = (unsigned long long)__double_as_longlong(d);
+  const int e = (int)((b >> 52) & 0x7FF);
+  const uint32_t low = (uint32_t)(b & 0x1FFFFFFFull);
+  if (e > 1023 - 126 && e < 1023 + 127 && (low - 0x10000000u + 16u) > 32u) return (float)d;
+  return (float)(a / t);
+}
+
+// Sum over the 1024 threads in a fixed order (the same value in every run).
+__device__ __forceinline__ double block_sum_f64_1024(double v, double* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < 32; ++w) t += sh[w];
+  __syncthreads();
+  return t;
+}
+
+// Exclusive scan over the 1024 threads (sh: 32 scratch entries); *total = block sum.
+template <typename T>
+__device__ __forceinline__ T tp_excl_scan(T v, T* sh, T* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  T x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sh[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    T s = sh[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    sh[lane] = s;
+  }
+  __syncthreads();
+  const T off = w ? sh[w - 1] : T(0);
+  if (total) *total = sh[31];
+  __syncthreads();
+  return off + x - v;
+}
+
+__device__ __forceinline__ int tp_block_min(int v, int* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int x = sh[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = min(x, __shfl_xor_sync(0xffffffffu, x, o));
+    if (threadIdx.x == 0) sh[0] = x;
+  }
+  __syncthreads();
+  const int r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+// ceil(u * x) exactly, for u in [0, 1) and x < 2^64.
+__device__ __forceinline__ unsigned long long tp_ceil_mul(double u, unsigned long long x) {
+  if (!(u > 0.0) || x == 0) return 0;
+  const unsigned long long b = (unsigned long long)__double_as_longlong(u);
+  const int e = (int)((b >> 52) & 0x7FF);
+  const unsigned long long m = (b & ((1ull << 52) - 1)) | (e ? (1ull << 52) : 0ull);
+  const int shift = (e ? 1075 - e : 1074);    // u = m * 2^-shift, shift >= 53
+  const unsigned long long lo = m * x, hi = __umul64hi(m, x);
+  if (shift >= 128) return (lo | hi) ? 1ull : 0ull;
+  unsigned long long q;
+  bool rem;
+  if (shift >= 64) {
+    const int s = shift - 64;
+    q = s ? (hi >> s) : hi;
+    rem = lo != 0 || (s && (hi & ((1ull << s) - 1)) != 0);
+  } else {
+    q = (hi << (64 - shift)) | (lo >> shift);
+    rem = (lo & ((1ull << shift) - 1)) != 0;
+  }
+  return q + (rem ? 1ull : 0ull);
+}
+
+struct TpPos {
+  int idx;                      // row index at the position (-1: the total never reaches the target)
+  unsigned long long incl;      // running sum up to and including it
+};
+
+// Inside a group of c > kTpRankMax row indices `a` (one first digit; the running sum
+// reaches target inside it, after `before` for the earlier groups): regroup by key
+// bits 18..9, then by bits 8..0 (counting sorts), each time keeping the subgroup in
+// which the running sum reaches target; the last subgroup holds one key, and in it
+// the m-th element in index order is the answer (found by a scan of the whole row).
+__device__ TpPos tp_select_deep(TopPSmem& s, const uint16_t* a, int c, unsigned long long before,
+                                unsigned long long target) {
+  __shared__ int shi[32];
+  __shared__ uint32_t shu[32];
+  __shared__ unsigned long long shs[32];
+  __shared__ unsigned long long s_before;
+  __shared__ int s_idx;
+  const int t = threadIdx.x;
+  const uint16_t* src = a;
+#pragma unroll 1
+  for (int level = 0; level < 2; ++level) {
+    const int shift = level == 0 ? 9 : 0, nb = level == 0 ? 1024 : 512;
+    uint16_t* dst = level == 0 ? s.deep : s.order;
+    if (t < nb) s.sub_cnt[t] = 0;
+    __syncthreads();
+    for (int x = t; x < c; x += 1024) atomicAdd(&s.sub_cnt[(s.key[src[x]] >> shift) & (nb - 1)], 1u);
+    __syncthreads();
+    const uint32_t mine = t < nb ? s.sub_cnt[t] : 0u;
+    const uint32_t o = tp_excl_scan<uint32_t>(mine, shu, nullptr);
+    if (t < nb) { s.sub_off[t] = o; s.sub_cnt[t] = 0; }
+    __syncthreads();
+    for (int x = t; x < c; x += 1024) {
+      const uint16_t i = src[x];
+      const int d = (s.key[i] >> shift) & (nb - 1);
+      dst[s.sub_off[d] + atomicAdd(&s.sub_cnt[d], 1u)] = i;
+    }
+    __syncthreads();
+    // running sums over the regrouped indices: thread t holds [t*per, t*per + per)
+    const int per = (c + 1023) / 1024, x0 = min(c, t * per), x1 = min(c, t * per + per);
+    unsigned long long loc = 0;
+    for (int x = x0; x < x1; ++x) loc += tp_fixed(s.key[dst[x]]);
+    const unsigned long long ex = before + tp_excl_scan<unsigned long long>(loc, shs, nullptr);
+    unsigned long long run = ex;
+    int cand = 0x7fffffff;
+    for (int x = x0; x < x1; ++x) {
+      run += tp_fixed(s.key[dst[x]]);
+      if (run >= target) { cand = x; break; }
+    }
+    const int xpos = tp_block_min(cand, shi);
+    if (xpos == 0x7fffffff) return TpPos{-1, 0};   // not reached (uniform across the block)
+    const int d = (s.key[dst[xpos]] >> shift) & (nb - 1);
+    const int st = (int)s.sub_off[d];
+    const int cn = (int)s.sub_cnt[d];
+    if (x0 <= st && st < x1) {
+      unsigned long long acc = ex;
+      for (int x = x0; x < st; ++x) acc += tp_fixed(s.key[dst[x]]);
+      s_before = acc;
+    }
+    __syncthreads();
+    before = s_before;
+    src = dst + st;
+    c = cn;
+    __syncthreads();
+  }
+  // one key left: its m-th element in index order reaches the target
+  const uint32_t key = s.key[src[0]];
+  const unsigned long long q = tp_fixed(key), tg = target - before;
+  unsigned long long m = (q == 0 || tg == 0) ? 1ull : (tg + q - 1) / q;
+  if (m > (unsigned long long)c) m = c;
+  int cm = 0;
+#pragma unroll 4
+  for (int j = 0; j < kTpPer; ++j) cm += s.key[t * kTpPer + j] == key;
+  int total;
+  const int exm = tp_excl_scan<int>(cm, shi, &total);
+  if ((unsigned long long)exm < m && m <= (unsigned long long)(exm + cm)) {
+    int r = (int)(m - exm);
+    for (int j = 0; j < kTpPer; ++j)
+      if (s.key[t * kTpPer + j] == key && --r == 0) { s_idx = t * kTpPer + j; break; }
+  }
+  __syncthreads();
+  const TpPos res{s_idx, before + m * q};
+  __syncthreads();
+  return res;
+}
+
+// First position of the reference's sorted order whose running sum reaches target.
+// pre = this thread's exclusive prefix over the grouped row (positions [t*kTpPer, ...)).
+__device__ TpPos tp_select(TopPSmem& s, int n, unsigned long long pre, unsigned long long target) {
+  __shared__ int shi[32];
+  __shared__ unsigned long long shs[32];
+  __shared__ unsigned long long s_before, s_incl;
+  __shared__ int s_idx;
+  const int t = threadIdx.x;
+  // the group: the one holding the first grouped position whose running sum reaches target
+  unsigned long long run = pre;
+  int cand = 0x7fffffff;
+#pragma unroll 4
+  for (int j = 0; j < kTpPer; ++j) {
+    const int pos = t * kTpPer + j;
+    if (pos < n) {
+      run += tp_fixed(s.key[s.by_digit[pos]]);
+      if (cand == 0x7fffffff && run >= target) cand = pos;
+    }
+  }
+  const int ipos = tp_block_min(cand, shi);
+  if (ipos == 0x7fffffff) return TpPos{-1, 0};
+  const uint32_t digit = s.key[s.by_digit[ipos]] >> 19;
+  const int start = (int)s.off[digit], c = (int)s.off[digit + 1] - start;
+  if (t == start / kTpPer) {
+    unsigned long long acc = pre;
+    for (int pos = t * kTpPer; pos < start; ++pos) acc += tp_fixed(s.key[s.by_digit[pos]]);
+    s_before = acc;
+  }
+  __syncthreads();
+  const unsigned long long before = s_before;
+  if (c > kTpRankMax) return tp_select_deep(s, s.by_digit + start, c, before, target);
+  // exact order inside the group: rank of (key, index) among the group, one warp per element
+  for (int x = t; x < c; x += 1024) {
+    const uint32_t ix = s.by_digit[start + x];
+    s.pk[x] = ((unsigned long long)s.key[ix] << 16) | ix;
+  }
+  __syncthreads();
+  const int lane = t & 31, w = t >> 5;
+  for (int x = w; x < c; x += 32) {
+    const unsigned long long kx = s.pk[x];
+    uint32_t r = 0;
+    for (int y = lane; y < c; y += 32) r += s.pk[y] < kx;
+    r = __reduce_add_sync(0xffffffffu, r);
+    if (lane == 0) s.order[r] = (uint16_t)(kx & 0xFFFF);
+  }
+  __syncthreads();
+  // running sums inside the group (one element per thread)
+  const unsigned long long v = t < c ? tp_fixed(s.key[s.order[t]]) : 0ull;
+  const unsigned long long ex = tp_excl_scan<unsigned long long>(v, shs, nullptr);
+  const int hit = (t < c && before + ex + v >= target) ? t : 0x7fffffff;
+  const int first = tp_block_min(hit, shi);
+  if (t == first) { s_idx = s.order[t]; s_incl = before + ex + v; }
+  __syncthreads();
+  const TpPos res{s_idx, s_incl};
+  __syncthreads();
+  return res;
+}
+
+// Returns the sampled index (all threads).  1 <= n <= kSortN.
+__device__ int top_p_sample_block(const float* logits, int n, int valid_lo, int valid_hi, double top_p,
+                                  double temperature, double u, TopPSmem& s) {
+  __shared__ double shd[32];
+  __shared__ float shf[32];
+  __shared__ unsigned long long shs[32];
+  __shared__ uint32_t shu[32];
+  const int t = threadIdx.x;
+  for (int b = t; b < kTpDigits; b += 1024) s.cnt[b] = 0;
+  // this thread's logits (masked ones -Inf); the maximum of the scaled logits:
+  // f32(x / t) does not decrease with x, so it is the scaled maximum logit
+  float lg[kTpPer];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kTpPer; ++j) {
+    const int i = t * kTpPer + j;
+    lg[j] = (i < n && i >= valid_lo && i < valid_hi) ? logits[i] : -INFINITY;
+    mx = fmaxf(mx, lg[j]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((t & 31) == 0) shf[t >> 5] = mx;
+  __syncthreads();
+  mx = shf[0];
+  for (int w = 1; w < 32; ++w) mx = fmaxf(mx, shf[w]);
+  const double max_scaled = (double)(float)((double)mx / temperature);
+  const double rt = 1.0 / temperature;
+  // exponentials (f32 values, f64 arithmetic) and their f64 sum
+  double part = 0.0;
+#pragma unroll
+  for (int j = 0; j < kTpPer; ++j) {
+    float v = 0.f;
+    if (lg[j] != -INFINITY) {
+      const float sc = tp_div_f32((double)lg[j], rt, temperature);
+      if (sc != -INFINITY) v = (float)exp((double)sc - max_scaled);
+    }
+    s.key[t * kTpPer + j] = __float_as_uint(v);
+    part += (double)v;
+  }
+  const double sum = block_sum_f64_1024(part, shd);
+  const double rs = 1.0 / sum;
+  // keys and first-digit counts
+  unsigned long long tot = 0;
+#pragma unroll 4
+  for (int j = 0; j < kTpPer; ++j) {
+    const int i = t * kTpPer + j;
+    uint32_t k = kTpNone;
+    if (i < n) {
+      const float pr = tp_div_f32((double)__uint_as_float(s.key[i]), rs, sum);
+      k = 0x7FFFFFFFu - (pr > 0.f ? __float_as_uint(pr) : 0u);   // NaN (no finite logit) counts as 0
+      atomicAdd(&s.cnt[k >> 19], 1u);
+      tot += tp_fixed(k);
+    }
+    s.key[i] = k;
+  }
+  __syncthreads();
+  // digit offsets (thread t owns digits [4t, 4t + 4)), then the grouped row
+  uint32_t c4[4], loc = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { c4[i] = s.cnt[4 * t + i]; loc += c4[i]; }
+  uint32_t o = tp_excl_scan<uint32_t>(loc, shu, nullptr);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { s.off[4 * t + i] = o; o += c4[i]; s.cnt[4 * t + i] = 0; }
+  if (t == 0) s.off[kTpDigits] = (uint32_t)n;
+  __syncthreads();
+#pragma unroll 4
+  for (int j = 0; j < kTpPer; ++j) {
+    const int i = t * kTpPer + j;
+    if (i < n) {
+      const uint32_t d = s.key[i] >> 19;
+      s.by_digit[s.off[d] + atomicAdd(&s.cnt[d], 1u)] = (uint16_t)i;
+    }
+  }
+  __syncthreads();
+  unsigned long long loc_sum = 0;
+#pragma unroll 4
+  for (int j = 0; j < kTpPer; ++j) {
+    const int pos = t * kTpPer + j;
+    if (pos < n) loc_sum += tp_fixed(s.key[s.by_digit[pos]]);
+  }
+  unsigned long long total;
+  const unsigned long long pre = tp_excl_scan<unsigned long long>(loc_sum, shs, &total);
+  // cutoff: the first position whose running sum reaches top_p (all n when none does)
+  const double tp_scaled = top_p * 9223372036854775808.0;
+  const unsigned long long t_cut = !(tp_scaled > 0.0) ? 0ull
+                                   : (tp_scaled >= 18446744073709551616.0 ? ~0ull : (unsigned long long)ceil(tp_scaled));
+  const TpPos cut = tp_select(s, n, pre, t_cut);
+  const unsigned long long re_sum = cut.idx >= 0 ? cut.incl : total;
+  // walk: the first position whose running sum reaches u * re_sum (at or before the cutoff)
+  TpPos pick = tp_select(s, n, pre, tp_ceil_mul(u, re_sum));
+  if (pick.idx < 0) pick = tp_select(s, n, pre, 0);
+  return pick.idx;
+}
+
+// Semantic code of the frame by top-p sampling when the slot samples (sample_mode 1);
+// the uniform draw is counter `frame` of the slot's sample_key stream.  Runs after
+// k_fm_prepare (which wrote the masked argmax) and replaces its choice.
+__global__ void __launch_bounds__(1024, 1) k_fm_sample(const __grid_constant__ FmParams p) {
+  extern __shared__ __align__(16) unsigned char tp_smem[];
+  griddep_launch();
+  griddep_wait();
+  SlotState& st = p.slots[p.slot];
+  if (st.sample_mode != 1) return;
+  const double u = vx_uniform01(st.sample_key, (uint64_t)st.frame);
+  const int n = min(p.sem_vocab, kSortN);
+  int idx = top_p_sample_block(p.head_out, n, 1, kSemValid, st.top_p, st.temperature, u,
+                               *reinterpret_cast<TopPSmem*>(tp_smem));
+  if (idx < 0 || idx >= n) idx = 0;   // only non-finite logits get here; keep the code a valid row
+  if (threadIdx.x == 0) {
+    st.codes[0] = (uint32_t)idx;
+    if (st.frame >= 0 && st.frame < st.max_frames)
+      p.code_ring[((long long)p.slot * st.max_frames + st.frame) * 37] = (uint32_t)idx;
+  }
+}
+
+// Test support: top-p sampling of a logit row, CTA b with the uniform draw u[b].
+__global__ void __launch_bounds__(1024, 1) k_top_p_test(const float* logits, int n, int valid_lo, int valid_hi,
+                                                     double top_p, double temperature, const double* u, int32_t* out) {
+  extern __shared__ __align__(16) unsigned char tp_smem[];
+  const int idx = top_p_sample_block(logits, n, valid_lo, valid_hi, top_p, temperature, u[blockIdx.x],
+                                     *reinterpret_cast<TopPSmem*>(tp_smem));
+  if (threadIdx.x == 0) out[blockIdx.x] = idx;
 }
 
 // x_proj = input_projection . x_t, and the two 3-token sequences

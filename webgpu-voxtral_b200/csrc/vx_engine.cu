@@ -251,6 +251,8 @@ int prime_kernel_attrs(vx_handle* h) {
   CK(cudaFuncSetAttribute(mk::k_decode_steps<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
   CK(cudaFuncSetAttribute(mk::k_decode_steps<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
   CK(cudaFuncSetAttribute(mk::k_decode_steps<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(k_fm_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem));
+  CK(cudaFuncSetAttribute(k_top_p_test, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem));
   CK(tc_attr<64>()); CK(tc_attr<128>()); CK(tc_attr<256>());
   return VX_OK;
 }
@@ -535,6 +537,7 @@ int enqueue_fm(vx_handle* h, int slot) {
   }
   FmParams f = fm_params(h, slot);
   CK(launch(h, k_fm_prepare, dim3(1), dim3(1024), 0, f));
+  CK(launch(h, k_fm_sample, dim3(1), dim3(1024), kSampleSmem, f));   // returns at once unless the slot samples
   const int steps = h->cfg.fm_nfe - 1;
   for (int s = 0; s < steps; ++s) {
     f.step = s;
@@ -1245,6 +1248,41 @@ int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, 
   return rc;
 }
 
+// Test support: the device top-p sampler (k_top_p_test) on a host logit row with
+// explicit uniform draws, one CTA per draw.
+int vx_selftest_top_p(vx_handle* h, const float* logits, int32_t n, int32_t valid_lo, int32_t valid_hi, double top_p,
+                      double temperature, const double* u, int32_t n_draws, int32_t* out) {
+  if (!h || !logits || !u || !out) return VX_E_INVALID;
+  if (n < 1 || n > kSortN || n_draws < 1 || n_draws > 65535 || !(temperature > 0) || !std::isfinite(temperature) ||
+      !std::isfinite(top_p))
+    return h->fail(VX_E_INVALID, "top-p selftest n=%d draws=%d", n, n_draws);
+  for (int i = 0; i < n_draws; ++i)
+    if (!(u[i] >= 0.0 && u[i] < 1.0)) return h->fail(VX_E_INVALID, "draw %d = %g outside [0, 1)", i, u[i]);
+  CK(cudaSetDevice(h->dev));
+  float* dl = nullptr;
+  double* du = nullptr;
+  int32_t* dout = nullptr;
+  int rc = VX_OK;
+  if (cudaMalloc(&dl, (size_t)n * 4) != cudaSuccess || cudaMalloc(&du, (size_t)n_draws * 8) != cudaSuccess ||
+      cudaMalloc(&dout, (size_t)n_draws * 4) != cudaSuccess)
+    rc = h->fail(VX_E_NOMEM, "selftest buffers");
+  if (!rc && (cudaMemcpyAsync(dl, logits, (size_t)n * 4, cudaMemcpyHostToDevice, h->stream) != cudaSuccess ||
+              cudaMemcpyAsync(du, u, (size_t)n_draws * 8, cudaMemcpyHostToDevice, h->stream) != cudaSuccess))
+    rc = h->fail(VX_E_CUDA, "selftest copy");
+  if (!rc) {
+    k_top_p_test<<<n_draws, 1024, kSampleSmem, h->stream>>>(dl, n, valid_lo, valid_hi, top_p, temperature, du, dout);
+    h->launches++;
+    if (cudaGetLastError() != cudaSuccess) rc = h->fail(VX_E_CUDA, "top-p selftest launch");
+  }
+  if (!rc && cudaMemcpyAsync(out, dout, (size_t)n_draws * 4, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess)
+    rc = h->fail(VX_E_CUDA, "selftest copy");
+  if (!rc) rc = finish(h);
+  cudaStreamSynchronize(h->stream);
+  for (void* ptr : {(void*)dl, (void*)du, (void*)dout})
+    if (ptr) cudaFree(ptr);
+  return rc;
+}
+
 int vx_set_stream(vx_handle* h, void* stream) {
   if (!h) return VX_E_INVALID;
   h->stream = stream ? (cudaStream_t)stream : h->own_stream;
@@ -1396,6 +1434,24 @@ int vx_set_streams(vx_handle* h, int32_t slot, uint64_t noise_seed, uint64_t cod
   u.codes_key = vx_stream_key(codes_seed, (uint64_t)utt);
   u.set_noise_mode = 1;
   u.noise_mode = 0;
+  if ((rc = slot_update(h, slot, u))) return rc;
+  return finish(h);
+}
+
+int vx_set_sampling(vx_handle* h, int32_t slot, int32_t mode, double top_p, double temperature, uint64_t seed) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (mode != 0 && mode != 1) return h->fail(VX_E_INVALID, "sampling mode %d (0 argmax, 1 top-p)", mode);
+  if (mode == 1 && !(std::isfinite(top_p) && std::isfinite(temperature) && temperature > 0))
+    return h->fail(VX_E_INVALID, "top_p %g / temperature %g", top_p, temperature);
+  if (mode == 1 && h->SEMV > kSortN) return h->fail(VX_E_RANGE, "semantic vocabulary %d > %d", h->SEMV, kSortN);
+  CK(cudaSetDevice(h->dev));
+  SlotUpdate u{};
+  u.set_sampling = 1;
+  u.sample_mode = mode;
+  u.top_p = top_p;
+  u.temperature = temperature;
+  u.sample_key = vx_stream_key(seed, kSampleStream);
   if ((rc = slot_update(h, slot, u))) return rc;
   return finish(h);
 }

@@ -55,6 +55,11 @@ VX_HD float vx_normal(uint64_t key, uint64_t i) {
   return (float)c * (1.0f / 131072.0f);     // power-of-two scale: exact
 }
 
+// Uniform double in [0, 1) from the top 53 bits of counter i (the sampler's draw).
+VX_HD double vx_uniform01(uint64_t key, uint64_t i) {
+  return (double)(vx_bits(key, i) >> 11) * (1.0 / 9007199254740992.0);
+}
+
 // Uniform integer in [lo, hi) (modulo bias < 2^-40 for the ranges used here).
 VX_HD uint32_t vx_uniform_int(uint64_t key, uint64_t i, uint32_t lo, uint32_t hi) {
   return lo + (uint32_t)(vx_bits(key, i) % (uint64_t)(hi - lo));

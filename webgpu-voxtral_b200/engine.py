@@ -106,6 +106,11 @@ def load_library():
         "vx_profile_step": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p,
                                            ctypes.POINTER(ctypes.c_double)]),
         "vx_trace": (ctypes.c_int, [H, ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t, _i32p]),
+        "vx_set_sampling": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_double, ctypes.c_double,
+                                           ctypes.c_uint64]),
+        "vx_selftest_top_p": (ctypes.c_int, [H, _f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_double,
+                                             ctypes.c_double, ctypes.POINTER(ctypes.c_double), ctypes.c_int32,
+                                             ctypes.POINTER(ctypes.c_int32)]),
         "vx_selftest_gemm": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             ctypes.c_int32, ctypes.c_uint64, ctypes.POINTER(ctypes.c_double)]),
         "vx_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p, _u8p]),
@@ -169,7 +174,9 @@ class VoxtralEngine:
         self._h = None
         self._ready = False
         self._sampling = o.get("sampling", "argmax")
-        self._rng = np.random.default_rng(o.get("samplingSeed", 0))
+        if self._sampling not in ("argmax", "top_p"):
+            raise ValueError(f"sampling {self._sampling!r}: 'argmax' or 'top_p'")
+        self._sampling_seed = int(o.get("samplingSeed", 0))
 
     # ------------------------------------------------------------------ lifecycle
     def _check(self, rc: int):
@@ -293,6 +300,16 @@ class VoxtralEngine:
     def set_streams(self, noise_seed: int = 3, codes_seed: int = 4, utt: int = 0, slot: int = 0):
         self._check(load_library().vx_set_streams(self._h, slot, noise_seed, codes_seed, utt))
 
+    def set_sampling(self, mode: str = "top_p", top_p: float = 0.9, temperature: float = 0.8, seed: int = 0,
+                     slot: int = 0):
+        """Semantic selection of the slot's FM frames on the device: 'argmax' (masked argmax)
+        or 'top_p' (sampleTopP, src/engine.ts:247-289, with the draw of frame f taken from
+        the seeded stream instead of Math.random)."""
+        if mode not in ("argmax", "top_p"):
+            raise ValueError(f"sampling mode {mode!r}")
+        self._check(load_library().vx_set_sampling(self._h, slot, int(mode == "top_p"), float(top_p),
+                                                   float(temperature), int(seed)))
+
     def set_stream(self, stream_ptr: Optional[int]):
         self._check(load_library().vx_set_stream(self._h, ctypes.c_void_p(stream_ptr or 0)))
 
@@ -321,6 +338,19 @@ class VoxtralEngine:
         err = (ctypes.c_double * 2)()
         self._check(load_library().vx_selftest_gemm(self._h, M, N, K, bn, max_splits, seed, err))
         return float(err[0]), float(err[1])
+
+    def selftest_top_p(self, logits, u, top_p: float = 0.9, temperature: float = 0.8, valid_lo: int = 0,
+                       valid_hi: Optional[int] = None) -> np.ndarray:
+        """Device top-p sampler on a logit row, one index per uniform draw in u."""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        uu = np.ascontiguousarray(u, dtype=np.float64).ravel()
+        out = np.empty(uu.size, np.int32)
+        hi = lg.size if valid_hi is None else valid_hi
+        self._check(load_library().vx_selftest_top_p(
+            self._h, _p(lg, _f32p), lg.size, valid_lo, hi, float(top_p), float(temperature),
+            uu.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), uu.size,
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return out
 
     def trace_arm(self):
         """Record phase timestamps of the next persistent-kernel launch (first 2 steps)."""
@@ -430,15 +460,17 @@ class VoxtralEngine:
                  eos: bool = True, slot: int = 0, chunk: int = 16) -> TTSResult:
         """generate() (src/engine.ts:2416-2616).
 
-        Prefill token by token (voice rows replace the [AUDIO] embeddings), the AUDIO
-        kick, then maxFrames frames.  Semantic selection is the masked argmax on the
-        device (sampling='argmax', the parity mode) or the reference's host top-p
-        sampler (sampling='top_p', temperature 0.8, p 0.9, seeded).  EOS (semantic
-        code <= 1) stops the loop as in the reference; frames are run on the device in
-        chunks and anything after EOS is discarded."""
+        Prefill (voice rows replace the [AUDIO] embeddings), the AUDIO kick, then
+        maxFrames frames on the device.  Semantic selection runs inside the FM graph:
+        the masked argmax (sampling='argmax', the parity mode) or the reference's
+        sampleTopP(0.9, 0.8) (sampling='top_p'; the draw of frame f comes from the
+        seeded stream samplingSeed, so a run is reproducible).  EOS (semantic code <= 1)
+        stops the loop as in the reference; frames are run in chunks and anything after
+        EOS is discarded."""
         self._require_ready()
         t0 = time.perf_counter()
         self.reset(slot)
+        self.set_sampling(self._sampling, 0.9, 0.8, self._sampling_seed, slot)
         if onStage:
             onStage("backbone")
         self.prefill(tokens, audioTokenStart, audioTokenCount, voiceEmbeddings, slot)
@@ -448,38 +480,22 @@ class VoxtralEngine:
             onStage("backbone", (t_prefill - t0) * 1e3)
             onStage("fm")
         sem_codes, ac_codes = [], []
-        if self._sampling == "top_p":
-            for f in range(maxFrames):
-                if f > 0:
-                    self.backboneStepCodes(sem_codes[-1], ac_codes[-1], slot)
-                r = self.debugFMStep(None, slot)
-                lg = r["semantic_logits"].astype(np.float64)
-                lg[0] = -np.inf
-                lg[8194:] = -np.inf
-                code = sample_top_p(lg, 0.9, 0.8, self._rng)
+        f = 0
+        done = False
+        while f < maxFrames and not done:
+            n = min(chunk, maxFrames - f)
+            self.decode(n, with_fm=True, slot=slot)
+            codes = self.read_codes(f, n, slot)
+            for i in range(n):
+                code = int(codes[i, 0])
                 if eos and code <= 1:
+                    done = True
                     break
                 sem_codes.append(code)
-                ac_codes.append(r["acoustic_codes"].astype(np.int64))
+                ac_codes.append(codes[i, 1:].astype(np.int64))
                 if onFrame:
-                    onFrame(f, code, r["acoustic_codes"])
-        else:
-            f = 0
-            done = False
-            while f < maxFrames and not done:
-                n = min(chunk, maxFrames - f)
-                self.decode(n, with_fm=True, slot=slot)
-                codes = self.read_codes(f, n, slot)
-                for i in range(n):
-                    code = int(codes[i, 0])
-                    if eos and code <= 1:
-                        done = True
-                        break
-                    sem_codes.append(code)
-                    ac_codes.append(codes[i, 1:].astype(np.int64))
-                    if onFrame:
-                        onFrame(f + i, code, codes[i, 1:])
-                f += n
+                    onFrame(f + i, code, codes[i, 1:])
+            f += n
         t_gen = time.perf_counter()
         if onStage:
             onStage("fm", (t_gen - t_prefill) * 1e3)
@@ -487,23 +503,6 @@ class VoxtralEngine:
             semanticCodes=sem_codes, acousticCodes=[a.tolist() for a in ac_codes], audio=np.zeros(0, np.float32),
             stats={"backboneMs": (t_prefill - t0) * 1e3, "fmMs": (t_gen - t_prefill) * 1e3, "codecMs": 0.0,
                    "totalMs": (t_gen - t0) * 1e3, "framesGenerated": len(sem_codes)})
-
-
-def sample_top_p(logits: np.ndarray, top_p: float, temperature: float, rng) -> int:
-    """sampleTopP (src/engine.ts:247-289) with a seeded generator in place of Math.random."""
-    scaled = logits / temperature
-    m = np.max(scaled)
-    p = np.exp(scaled - m)
-    p /= p.sum()
-    order = np.argsort(-p, kind="stable")
-    cum = np.cumsum(p[order])
-    cutoff = int(np.searchsorted(cum, top_p) + 1)
-    cutoff = min(cutoff, len(order))
-    keep = order[:cutoff]
-    r = rng.random() * p[keep].sum()
-    acc = np.cumsum(p[keep])
-    idx = int(np.searchsorted(acc, r))
-    return int(keep[min(idx, cutoff - 1)])
 
 
 def header_symbols() -> list:

@@ -59,6 +59,19 @@ def bits(key: int, idx: np.ndarray) -> np.ndarray:
         return _splitmix64(np.uint64(key) ^ (idx * np.uint64(0x9FB21C651E98DF25)))
 
 
+def uniform01(key: int, idx) -> np.ndarray:
+    """Uniform double in [0, 1) from the top 53 bits, bit-identical to vx_uniform01()."""
+    return (bits(key, idx) >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
+
+
+SAMPLE_STREAM = 0x73616D706C65   # stream id of the device sampler's draws ("sample")
+
+
+def sample_key(seed: int) -> int:
+    """Key of vx_set_sampling(seed): the draw of frame f is uniform01(sample_key(seed), f)."""
+    return stream_key(seed, SAMPLE_STREAM)
+
+
 def normal(key: int, idx: np.ndarray) -> np.ndarray:
     """Irwin-Hall-12 approximate N(0,1) in f32, bit-identical to vx_normal()."""
     idx = np.asarray(idx, dtype=np.uint64)
