@@ -60,6 +60,7 @@ typedef struct vx_config {
   int32_t enable_fm;   /* allocate the acoustic transformer */
   int32_t device;      /* CUDA device ordinal */
   int32_t tp_size, tp_rank; /* tensor parallelism (1 = off) */
+  int32_t enable_codec;     /* allocate the codec decoder (CodecConfig, src/types.ts:39-62) */
 } vx_config;
 
 /* defaultConfig (src/types.ts:70-122) with maxSeqLen 4096, 1 slot. */
@@ -235,6 +236,26 @@ int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t*
  * out_rel_err[2] = max|Y - Yref| / max|Yref| of the two passes. */
 int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, int32_t max_splits, uint64_t seed,
                      double* out_rel_err);
+
+/* Codec decoder, codecDecode(semanticCodes, acousticCodes) (src/engine.ts:1402-1713):
+ * sem[n_frames] semantic codes and ac[n_frames * 36] acoustic codes (as generate()
+ * produces them) -> audio[n_frames * 1920] f32 samples at 24 kHz.  VQ lookup (the
+ * raw semantic code indexes the 8192-entry codebook; codes >= 8192 give a zero row)
+ * + FSQ dequantisation, the causal input convolution, 4 stages of 2 transformer
+ * layers (windowed ALiBi attention, windows 2/4/8/16) with a stride-2 transposed
+ * convolution after stages 0-2, and the 7-tap output convolution.  1 <= n_frames <=
+ * 8192.  Needs enable_codec and loaded weights. */
+int vx_codec_decode(vx_handle* h, const uint32_t* sem, const uint32_t* ac, int32_t n_frames, float* audio);
+
+/* debugCodecDecode (src/engine.ts:1719-1975): the same decode with its intermediates,
+ * concatenated in this order into out[vx_codec_debug_size(n_frames)] (T = n_frames):
+ *   concat [T][292] (vq_embed | fsq_dequant), after_input_conv [T][1024],
+ *   after_stage0_transformer [T][1024], after_stage0_conv_up [2T][1024],
+ *   after_stage1_transformer [2T][1024], after_stage1_conv_up [4T][1024],
+ *   after_stage2_transformer [4T][1024], after_stage2_conv_up [8T][1024],
+ *   after_stage3_transformer [8T][1024], audio [8T][240]. */
+size_t vx_codec_debug_size(int32_t n_frames);
+int vx_codec_debug(vx_handle* h, const uint32_t* sem, const uint32_t* ac, int32_t n_frames, float* out, size_t n_out);
 
 /* Test support for the device top-p sampler (sampleTopP, src/engine.ts:247-289): the
  * logits[n] (n <= 16384) with indices outside [valid_lo, valid_hi) masked to -Inf, one

@@ -58,6 +58,14 @@ def lib():
                                    ctypes.c_int, _f32p, _u32p, ctypes.c_int, _u32p, _u32p, _f32p]
         L.orc_num_threads.restype = ctypes.c_int
         L.orc_set_threads.argtypes = [ctypes.c_int]
+        L.orc_codec_create.restype = ctypes.c_void_p
+        L.orc_codec_create.argtypes = []
+        L.orc_codec_destroy.argtypes = [ctypes.c_void_p]
+        L.orc_codec_set_tensor.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _u16p, ctypes.c_size_t]
+        L.orc_codec_get_tensor.argtypes = [ctypes.c_void_p, ctypes.c_char_p, _u16p, ctypes.c_size_t]
+        L.orc_codec_debug_size.restype = ctypes.c_size_t
+        L.orc_codec_debug_size.argtypes = [ctypes.c_int]
+        L.orc_codec_decode.argtypes = [ctypes.c_void_p, _u32p, _u32p, ctypes.c_int, _f32p, ctypes.c_size_t]
         _lib = L
     return _lib
 
@@ -166,3 +174,53 @@ def masked_argmax(x, valid=8194) -> int:
 def argmax_shader(x) -> int:
     a = np.ascontiguousarray(x, dtype=np.float32)
     return int(lib().orc_argmax_shader(_p(a, _f32p), len(a)))
+
+
+# Order and widths of the codec intermediates (debugCodecDecode, src/engine.ts:1719-1975);
+# rows = T * 2^stage.
+CODEC_ORDER = [("concat", 0, 292), ("after_input_conv", 0, 1024)] + [
+    item for s in range(4) for item in
+    [(f"after_stage{s}_transformer", s, 1024)] + ([(f"after_stage{s}_conv_up", s + 1, 1024)] if s < 3 else [])
+] + [("audio", 3, 240)]
+
+
+class Codec:
+    """CPU restatement of the codec decoder (oracle.cpp, orc_codec_*), synthetic weights."""
+
+    def __init__(self):
+        self._h = lib().orc_codec_create()
+
+    def close(self):
+        if self._h:
+            lib().orc_codec_destroy(self._h)
+            self._h = None
+
+    def set_tensor(self, name: str, f16_bits: np.ndarray):
+        a = np.ascontiguousarray(f16_bits, dtype=np.uint16).ravel()
+        rc = lib().orc_codec_set_tensor(self._h, name.encode(), a.ctypes.data_as(_u16p), a.size)
+        if rc:
+            raise KeyError(f"{name}: {rc}")
+
+    def tensor(self, name: str, n: int) -> np.ndarray:
+        out = np.empty(n, np.uint16)
+        rc = lib().orc_codec_get_tensor(self._h, name.encode(), out.ctypes.data_as(_u16p), n)
+        if rc:
+            raise KeyError(f"{name}: {rc}")
+        return out
+
+    def decode(self, sem, ac) -> dict:
+        sem = np.ascontiguousarray(sem, dtype=np.uint32).ravel()
+        ac = np.ascontiguousarray(ac, dtype=np.uint32).ravel()
+        T = sem.size
+        n = lib().orc_codec_debug_size(T)
+        buf = np.empty(n, np.float32)
+        rc = lib().orc_codec_decode(self._h, sem.ctypes.data_as(_u32p), ac.ctypes.data_as(_u32p), T,
+                                    buf.ctypes.data_as(_f32p), n)
+        if rc:
+            raise RuntimeError(f"orc_codec_decode: {rc}")
+        out, off = {}, 0
+        for name, s, w in CODEC_ORDER:
+            rows = (T << s) if name != "audio" else 8 * T
+            out[name] = buf[off: off + rows * w].reshape(rows, w)
+            off += rows * w
+        return out

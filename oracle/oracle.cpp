@@ -659,3 +659,299 @@ int orc_generate(orc_handle* h, const int32_t* tokens, int n_tokens, int audio_s
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Codec decoder: codecDecode (src/engine.ts:1402-1713) with the intermediates of
+// debugCodecDecode (:1719-1975).  Same conventions as above: f16 weight bits, f32
+// activations, the shaders' operation order.
+namespace {
+
+constexpr int kCDim = 1024, kCHidden = 4096, kCHeads = 8, kCHd = 128;
+
+struct CodecLayerW {
+  std::vector<uint16_t> wq, wk, wv, wo, w1, w2, w3, attn_norm, ffn_norm, q_norm, k_norm, attn_scale, ffn_scale;
+};
+
+struct CodecW {
+  std::vector<uint16_t> sem_sum, usage, in_v, in_g, out_v, out_g, up_v[3], up_g[3];
+  CodecLayerW L[8];
+  std::vector<uint16_t> cb;   // normalised codebook (f16)
+  std::vector<std::pair<std::string, std::vector<uint16_t>*>> named;
+};
+
+// Synthetic codec tensors: N(0, 0.02) matrices, or a constant for gains (1.0), the
+// layer scales (0.1) and the codebook usage counts (2.0) — the values the engine's
+// vx_init_random_weights writes.
+void gen_fill(CodecW& c, std::vector<uint16_t>& t, const std::string& name, size_t n, float fill) {
+  c.named.push_back({name, &t});
+  if (fill != 0.f) {
+    t.assign(n, vx_f32_to_f16_bits(fill));
+    return;
+  }
+  gen_tensor(t, name, n, false);
+}
+
+// normalizeCodebook (src/shaders.ts:856-888): f16(sum / max(usage, 1e-5)).
+void codec_normalize(CodecW& c) {
+  init_lut();
+  c.cb.resize(c.sem_sum.size());
+  for (size_t i = 0; i < c.sem_sum.size(); ++i) {
+    const float u = std::max(g_f16_lut[c.usage[i / 256]], 1e-5f);
+    c.cb[i] = vx_f32_to_f16_bits(g_f16_lut[c.sem_sum[i]] / u);
+  }
+}
+
+// causalConv1d (src/shaders.ts:919-979), [T, c] time-major, weight norm per output
+// channel: wNorm = 1/sqrt(sum over consecutive pairs of (a*a + b*b) + 1e-12), then
+// sum over ci (outer) and tap k (inner) of (w * wNorm * g) * x[t - (K-1) + k].
+void causal_conv1d(const float* in, int T, int c_in, int c_out, int K, const uint16_t* v, const uint16_t* g, float* out) {
+  init_lut();
+#pragma omp parallel for schedule(static)
+  for (int co = 0; co < c_out; ++co) {
+    const float gv = g_f16_lut[g[co]];
+    const uint16_t* w = v + (size_t)co * c_in * K;
+    float wn = 0.f;
+    for (int p = 0; p < c_in * K / 2; ++p) {
+      const float a = g_f16_lut[w[2 * p]], b = g_f16_lut[w[2 * p + 1]];
+      wn += a * a + b * b;
+    }
+    wn = 1.0f / sqrtf(wn + 1e-12f);
+    for (int t = 0; t < T; ++t) {
+      float sum = 0.f;
+      for (int ci = 0; ci < c_in; ++ci)
+        for (int k = 0; k < K; ++k) {
+          const int ti = t - (K - 1) + k;
+          if (ti >= 0) sum += (g_f16_lut[w[ci * K + k]] * wn * gv) * in[(size_t)ti * c_in + ci];
+        }
+      out[(size_t)t * c_out + co] = sum;
+    }
+  }
+}
+
+// convTransposeNormScale + causalConvTranspose1d (src/shaders.ts:1004-1104), stride 2,
+// 4 taps: scale[ci] = g[ci] / sqrt(sum of v[ci,:,:]^2 + 1e-12) (256-lane strided sums,
+// tree reduction); out[t][co] = sum over taps k with t - k even and >= 0 (outer) and
+// ci (inner) of (w[ci][co][k] * scale[ci]) * x[(t - k) / 2][ci].  T_out = 2 T_in.
+void conv_transpose(const float* in, int T_in, const uint16_t* v, const uint16_t* g, float* out) {
+  init_lut();
+  const int C = kCDim, K = 4;
+  std::vector<float> scale(C);
+  for (int ci = 0; ci < C; ++ci) {
+    float s[256];
+    const uint16_t* w = v + (size_t)ci * C * K;
+    for (int t = 0; t < 256; ++t) {
+      float ss = 0.f;
+      for (int i = t; i < C * K; i += 256) ss += g_f16_lut[w[i]] * g_f16_lut[w[i]];
+      s[t] = ss;
+    }
+    for (int st = 128; st > 0; st >>= 1)
+      for (int t = 0; t < st; ++t) s[t] += s[t + st];
+    scale[ci] = g_f16_lut[g[ci]] * (1.0f / sqrtf(s[0] + 1e-12f));
+  }
+  const int T_out = 2 * T_in;
+#pragma omp parallel for schedule(static)
+  for (int co = 0; co < C; ++co)
+    for (int t = 0; t < T_out; ++t) {
+      float sum = 0.f;
+      for (int k = 0; k < K; ++k) {
+        const int diff = t - k;
+        if (diff >= 0 && diff % 2 == 0) {
+          const int ti = diff / 2;
+          for (int ci = 0; ci < C; ++ci)
+            sum += (g_f16_lut[v[((size_t)ci * C + co) * K + k]] * scale[ci]) * in[(size_t)ti * C + ci];
+        }
+      }
+      out[(size_t)t * C + co] = sum;
+    }
+}
+
+// batchedMatvecF16 (src/shaders.ts:1586-1633) = matvecF16 per frame.
+void codec_matvec(const std::vector<uint16_t>& A, int M, int K, const float* x, int N, float* y) {
+  std::vector<const float*> xs(N);
+  std::vector<float*> ys(N);
+  for (int n = 0; n < N; ++n) { xs[n] = x + (size_t)n * K; ys[n] = y + (size_t)n * M; }
+  matvec_f16(A.data(), M, K, N, xs.data(), ys.data());
+}
+
+// qkNorm (src/shaders.ts:1795-1838), per (token, head): sequential sum of squares,
+// rms = 1/sqrt(ss/128 + 1e-6), x = x * rms * w[h*128 + d].
+void qk_norm(float* x, int N, const std::vector<uint16_t>& w) {
+  for (int r = 0; r < N * kCHeads; ++r) {
+    float* p = x + (size_t)r * kCHd;
+    const int h = r % kCHeads;
+    float ss = 0.f;
+    for (int d = 0; d < kCHd; ++d) ss += p[d] * p[d];
+    const float rms = 1.0f / sqrtf(ss / (float)kCHd + 1e-6f);
+    for (int d = 0; d < kCHd; ++d) p[d] = p[d] * rms * g_f16_lut[w[h * kCHd + d]];
+  }
+}
+
+// alibiAttnScore + codecSoftmax + codecAttnValue (src/shaders.ts:1432-1575).
+void codec_attention(const float* q, const float* k, const float* v, int N, int W, float* out) {
+  const float scale = 1.0f / sqrtf((float)kCHd);
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < kCHeads; ++h) {
+    const float slope = powf(2.0f, -8.0f * (float)(h + 1) / (float)kCHeads);
+    std::vector<float> sc(W);
+    for (int qi = 0; qi < N; ++qi) {
+      const int k0 = qi + 1 > W ? qi - W + 1 : 0;
+      for (int s = 0; s < W; ++s) {
+        const int ki = k0 + s;
+        if (ki > qi) { sc[s] = -1e30f; continue; }
+        float dot = 0.f;
+        for (int d = 0; d < kCHd; ++d) dot += q[((size_t)qi * kCHeads + h) * kCHd + d] * k[((size_t)ki * kCHeads + h) * kCHd + d];
+        sc[s] = dot * scale + (-slope * (float)(qi - ki));
+      }
+      float mx = -1e30f;
+      for (int s = 0; s < W; ++s) mx = std::max(mx, sc[s]);
+      float sum = 0.f;
+      for (int s = 0; s < W; ++s) { sc[s] = expf(sc[s] - mx); sum += sc[s]; }
+      for (int s = 0; s < W; ++s) sc[s] /= sum;
+      for (int d = 0; d < kCHd; ++d) {
+        float acc = 0.f;
+        for (int s = 0; s < W; ++s) {
+          const int ki = k0 + s;
+          if (ki > qi) break;
+          acc += sc[s] * v[((size_t)ki * kCHeads + h) * kCHd + d];
+        }
+        out[((size_t)qi * kCHeads + h) * kCHd + d] = acc;
+      }
+    }
+  }
+}
+
+// One decoder transformer layer over N tokens (src/engine.ts:1501-1646).
+void codec_layer(const CodecLayerW& L, std::vector<float>& cur, int N, int W) {
+  const size_t n = (size_t)N * kCDim;
+  std::vector<float> res(cur), nrm(n), q(n), k(n), v(n), att(n), o(n);
+  for (int t = 0; t < N; ++t) rms_norm(&cur[(size_t)t * kCDim], L.attn_norm.data(), kCDim, 0.01f, &nrm[(size_t)t * kCDim]);
+  codec_matvec(L.wq, kCDim, kCDim, nrm.data(), N, q.data());
+  codec_matvec(L.wk, kCDim, kCDim, nrm.data(), N, k.data());
+  codec_matvec(L.wv, kCDim, kCDim, nrm.data(), N, v.data());
+  qk_norm(q.data(), N, L.q_norm);
+  qk_norm(k.data(), N, L.k_norm);
+  codec_attention(q.data(), k.data(), v.data(), N, W, att.data());
+  codec_matvec(L.wo, kCDim, kCDim, att.data(), N, o.data());
+  for (size_t i = 0; i < n; ++i) cur[i] = o[i] * g_f16_lut[L.attn_scale[i % kCDim]] + res[i];
+  res = cur;
+  for (int t = 0; t < N; ++t) rms_norm(&cur[(size_t)t * kCDim], L.ffn_norm.data(), kCDim, 0.01f, &nrm[(size_t)t * kCDim]);
+  std::vector<float> gate((size_t)N * kCHidden), up((size_t)N * kCHidden);
+  codec_matvec(L.w1, kCHidden, kCDim, nrm.data(), N, gate.data());
+  codec_matvec(L.w3, kCHidden, kCDim, nrm.data(), N, up.data());
+  for (size_t i = 0; i < gate.size(); ++i) gate[i] = swiglu(gate[i], up[i]);
+  codec_matvec(L.w2, kCDim, kCHidden, gate.data(), N, o.data());
+  for (size_t i = 0; i < n; ++i) cur[i] = o[i] * g_f16_lut[L.ffn_scale[i % kCDim]] + res[i];
+}
+
+}  // namespace
+
+extern "C" {
+
+struct orc_codec {
+  CodecW w;
+};
+
+orc_codec* orc_codec_create(void) {
+  init_lut();
+  orc_codec* h = new orc_codec();
+  CodecW& c = h->w;
+  const std::string P = "audio_tokenizer.";
+  gen_fill(c, c.sem_sum, P + "quantizer.semantic_codebook.embedding_sum", (size_t)8192 * 256, 0.f);
+  gen_fill(c, c.usage, P + "quantizer.semantic_codebook.cluster_usage", 8192, 2.0f);
+  gen_fill(c, c.in_v, P + "decoder_blocks.0.conv.parametrizations.weight.original1", (size_t)kCDim * 292 * 3, 0.f);
+  gen_fill(c, c.in_g, P + "decoder_blocks.0.conv.parametrizations.weight.original0", kCDim, 1.0f);
+  for (int s = 0; s < 4; ++s)
+    for (int l = 0; l < 2; ++l) {
+      CodecLayerW& L = c.L[2 * s + l];
+      const std::string pre = P + "decoder_blocks." + std::to_string(1 + 2 * s) + ".layers." + std::to_string(l) + ".";
+      const size_t DD = (size_t)kCDim * kCDim, DF = (size_t)kCDim * kCHidden;
+      gen_fill(c, L.wq, pre + "attention.wq.weight", DD, 0.f);
+      gen_fill(c, L.wk, pre + "attention.wk.weight", DD, 0.f);
+      gen_fill(c, L.wv, pre + "attention.wv.weight", DD, 0.f);
+      gen_fill(c, L.wo, pre + "attention.wo.weight", DD, 0.f);
+      gen_fill(c, L.w1, pre + "feed_forward.w1.weight", DF, 0.f);
+      gen_fill(c, L.w3, pre + "feed_forward.w3.weight", DF, 0.f);
+      gen_fill(c, L.w2, pre + "feed_forward.w2.weight", DF, 0.f);
+      gen_fill(c, L.attn_norm, pre + "attention_norm.weight", kCDim, 1.0f);
+      gen_fill(c, L.ffn_norm, pre + "ffn_norm.weight", kCDim, 1.0f);
+      gen_fill(c, L.q_norm, pre + "attention.q_norm.weight", kCDim, 1.0f);
+      gen_fill(c, L.k_norm, pre + "attention.k_norm.weight", kCDim, 1.0f);
+      gen_fill(c, L.attn_scale, pre + "attention_scale", kCDim, 0.1f);
+      gen_fill(c, L.ffn_scale, pre + "ffn_scale", kCDim, 0.1f);
+    }
+  for (int s = 0; s < 3; ++s) {
+    const std::string pre = P + "decoder_blocks." + std::to_string(2 + 2 * s) + ".conv.parametrizations.weight.";
+    gen_fill(c, c.up_v[s], pre + "original1", (size_t)kCDim * kCDim * 4, 0.f);
+    gen_fill(c, c.up_g[s], pre + "original0", kCDim, 1.0f);
+  }
+  gen_fill(c, c.out_v, P + "output_proj.conv.parametrizations.weight.original1", (size_t)240 * kCDim * 7, 0.f);
+  gen_fill(c, c.out_g, P + "output_proj.conv.parametrizations.weight.original0", 240, 1.0f);
+  codec_normalize(c);
+  return h;
+}
+
+void orc_codec_destroy(orc_codec* h) { delete h; }
+
+// Replace one tensor (f16 bits, full size) — e.g. to mirror a checkpoint loaded into the engine.
+int orc_codec_set_tensor(orc_codec* h, const char* name, const uint16_t* data, size_t n) {
+  for (auto& kv : h->w.named)
+    if (kv.first == name) {
+      if (kv.second->size() != n) return -2;
+      memcpy(kv.second->data(), data, n * 2);
+      codec_normalize(h->w);
+      return 0;
+    }
+  return -1;
+}
+
+int orc_codec_get_tensor(orc_codec* h, const char* name, uint16_t* out, size_t n) {
+  for (auto& kv : h->w.named)
+    if (kv.first == name) {
+      if (kv.second->size() != n) return -2;
+      memcpy(out, kv.second->data(), n * 2);
+      return 0;
+    }
+  return -1;
+}
+
+size_t orc_codec_debug_size(int T) { return T < 1 ? 0 : (size_t)T * (292 + 30 * kCDim + 8 * 240); }
+
+// The decode with the intermediates in the engine's vx_codec_debug order (concat,
+// after_input_conv, per stage the transformer output and the upsampled output, audio).
+int orc_codec_decode(orc_codec* h, const uint32_t* sem, const uint32_t* ac, int T, float* out, size_t n_out) {
+  if (T < 1 || n_out != orc_codec_debug_size(T)) return -1;
+  const CodecW& c = h->w;
+  size_t off = 0;
+  auto dump = [&](const float* p, size_t n) { memcpy(out + off, p, n * 4); off += n; };
+  // vqLookup + fsqDequant + concat (src/shaders.ts:817-848, 890-917, 1840-1867)
+  std::vector<float> x0((size_t)T * 292);
+  for (int t = 0; t < T; ++t) {
+    for (int d = 0; d < 256; ++d)
+      x0[(size_t)t * 292 + d] = sem[t] < 8192 ? g_f16_lut[c.cb[(size_t)sem[t] * 256 + d]] : 0.f;
+    for (int i = 0; i < 36; ++i) {
+      const uint32_t code = ac[(size_t)t * 36 + i] - 2u;
+      x0[(size_t)t * 292 + 256 + i] = (float)code * 2.0f / 20.0f - 1.0f;
+    }
+  }
+  dump(x0.data(), x0.size());
+  std::vector<float> cur((size_t)T * kCDim);
+  causal_conv1d(x0.data(), T, 292, kCDim, 3, c.in_v.data(), c.in_g.data(), cur.data());
+  dump(cur.data(), cur.size());
+  for (int s = 0; s < 4; ++s) {
+    const int N = T << s, W = 2 << s;
+    for (int l = 0; l < 2; ++l) codec_layer(c.L[2 * s + l], cur, N, W);
+    dump(cur.data(), cur.size());
+    if (s < 3) {
+      std::vector<float> up((size_t)2 * N * kCDim);
+      conv_transpose(cur.data(), N, c.up_v[s].data(), c.up_g[s].data(), up.data());
+      cur.swap(up);
+      dump(cur.data(), cur.size());
+    }
+  }
+  std::vector<float> audio((size_t)8 * T * 240);
+  causal_conv1d(cur.data(), 8 * T, kCDim, 240, 7, c.out_v.data(), c.out_g.data(), audio.data());
+  dump(audio.data(), audio.size());
+  return off == n_out ? 0 : -3;
+}
+
+}  // extern "C"

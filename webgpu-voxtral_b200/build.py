@@ -17,7 +17,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libvoxtral_b200.so")
 SOURCES = ["vx_engine.cu", "vx_noalloc.cu"]
-DEPS = ["vx_engine.cu", "vx_noalloc.cu", "k_gemv.cuh", "k_attn.cuh", "k_misc.cuh", "k_step.cuh", "vx_common.cuh", "vx_rng.h"]
+DEPS = ["vx_engine.cu", "vx_noalloc.cu", "k_gemv.cuh", "k_attn.cuh", "k_misc.cuh", "k_step.cuh", "k_gemm.cuh", "k_codec.cuh",
+        "vx_codec.cuh", "vx_common.cuh", "vx_rng.h"]
 
 
 def nvcc() -> str:

@@ -27,6 +27,7 @@
 
 #include "../../include/voxtral_b200.h"
 #include "k_attn.cuh"
+#include "k_codec.cuh"
 #include "k_gemm.cuh"
 #include "k_gemv.cuh"
 #include "k_misc.cuh"
@@ -51,6 +52,7 @@ struct TensorSlot {
   long long full_rows, full_cols;
   long long row0, col0;       // block origin inside the full tensor
   bool is_norm;
+  float fill = 0.f;           // synthetic weights: 0 = N(0, sigma) values, else this constant
 };
 
 struct NcclApi {
@@ -78,6 +80,8 @@ NcclApi g_nccl;
 
 }  // namespace
 
+struct CodecState;   // vx_codec.cuh
+
 struct vx_handle {
   vx_config cfg{};
   int dev = 0, num_sms = 148;
@@ -99,6 +103,7 @@ struct vx_handle {
   __half *fm_in = nullptr, *fm_head = nullptr, *fm_time = nullptr, *fm_norm = nullptr, *fm_ac = nullptr;
   std::unordered_map<std::string, TensorSlot> tensors;
   bool weights_ready = false, tp_table_ready = false;
+  CodecState* codec = nullptr;   // codec decoder (vx_codec.cuh), when enabled
 
   // KV cache
   __half* kv_pool = nullptr;
@@ -660,8 +665,9 @@ int slot_update(vx_handle* h, int slot, const SlotUpdate& u) {
 // when the output has fewer tiles than SMs: floor(SMs / tiles) splits (at most
 // `max_splits`), so that the CTAs form one whole wave.
 template <int BN>
-int run_tc_gemm(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo, float* y,
-                long long ldy, int M, int N, int K, int accumulate, int max_splits = 8, int* splits_out = nullptr) {
+int run_tc_gemm_ws(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo, float* y,
+                   long long ldy, int M, int N, int K, int accumulate, float* ws, size_t ws_floats, int max_splits = 8,
+                   int* splits_out = nullptr) {
   if (N < 1 || M < 1 || K < tc::kBK || K % tc::kBK) return h->fail(VX_E_INVALID, "tensor-core GEMM shape %dx%dx%d", M, N, K);
   const int n_tiles = (N + BN - 1) / BN, m_tiles = (M + tc::kBM - 1) / tc::kBM;
   const int chunks = K / tc::kBK;
@@ -669,20 +675,27 @@ int run_tc_gemm(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, cons
   int splits = 1;
   if (tiles < h->num_sms) splits = std::max(1, std::min({chunks, max_splits, h->num_sms / tiles}));
   if (M % 4 || ldy % 4) splits = 1;   // the split-K reduction writes float4 along m
-  while (splits > 1 && (size_t)tiles * splits * BN * tc::kBM > h->tb_ws_floats) --splits;
+  while (splits > 1 && (size_t)tiles * splits * BN * tc::kBM > ws_floats) --splits;
   const int cps = (chunks + splits - 1) / splits;
   splits = (chunks + cps - 1) / cps;
-  tc::Params p{y, ldy, h->tb_ws, M, N, K, cps, accumulate};
+  tc::Params p{y, ldy, ws, M, N, K, cps, accumulate};
   CK(launch(h, tc::k_gemm<BN>, dim3(n_tiles, m_tiles, splits), dim3(tc::kThreads), tc::Cfg<BN>::kSmem, w, xhi, xlo, p));
   if (splits_out) {
     *splits_out = splits > 1 ? splits : 0;   // the caller's row kernel sums the partials
   } else if (splits > 1) {
-    tc::ReduceParams rp{h->tb_ws, y, ldy, M, N, splits, n_tiles, BN, accumulate};
+    tc::ReduceParams rp{ws, y, ldy, M, N, splits, n_tiles, BN, accumulate};
     const long long n4 = (long long)N * (M / 4);
     CK(launch(h, tc::k_splitk_reduce, dim3((unsigned)std::min<long long>((n4 + 255) / 256, 4L * h->num_sms)), dim3(256),
               0, rp));
   }
   return VX_OK;
+}
+
+template <int BN>
+int run_tc_gemm(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, const CUtensorMap& xlo, float* y,
+                long long ldy, int M, int N, int K, int accumulate, int max_splits = 8, int* splits_out = nullptr) {
+  return run_tc_gemm_ws<BN>(h, w, xhi, xlo, y, ldy, M, N, K, accumulate, h->tb_ws, h->tb_ws_floats, max_splits,
+                            splits_out);
 }
 
 // Per-row epilogue launch (k_tb_row): split-K sum + residual + RMSNorm -> hi/lo, or
@@ -895,6 +908,8 @@ int finish(vx_handle* h) {
 
 }  // namespace
 
+#include "vx_codec.cuh"
+
 // ============================================================================
 // C ABI
 // ============================================================================
@@ -908,6 +923,7 @@ void vx_default_config(vx_config* c) {
   c->acoustic_levels = 21; c->audio_vocab = 9088;
   c->max_seq_len = 4096; c->max_slots = 1; c->max_frames = 2048; c->max_voice_rows = 256;
   c->enable_fm = 1; c->device = 0; c->tp_size = 1; c->tp_rank = 0;
+  c->enable_codec = 1;
 }
 
 const char* vx_last_error(const vx_handle* h) { return h ? h->err.c_str() : "null handle"; }
@@ -916,7 +932,7 @@ int64_t vx_launch_count(const vx_handle* h) { return h ? h->launches : 0; }
 
 static void add_tensor(vx_handle* h, const std::string& name, __half* dst, long long ld, long long rows, long long cols,
                        long long full_rows, long long full_cols, long long row0, long long col0, bool norm) {
-  h->tensors[name] = TensorSlot{dst, ld, rows, cols, full_rows, full_cols, row0, col0, norm};
+  h->tensors[name] = TensorSlot{dst, ld, rows, cols, full_rows, full_cols, row0, col0, norm, norm ? 1.0f : 0.f};
 }
 
 int vx_create(const vx_config* cfg, vx_handle** out) {
@@ -1035,6 +1051,7 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     add_tensor(h, p + "norm.weight", h->fm_norm, D, 1, D, 1, D, 0, 0, true);
     add_tensor(h, p + "acoustic_codebook_output.weight", h->fm_ac, D, 36, D, 36, D, 0, 0, false);
   }
+  if (c.enable_codec && (rc = codec_create(h))) { *out = h; return rc; }
 
   // ---------------------------------------------------------- KV cache + activations
   h->max_pages = (c.max_seq_len + kPage - 1) / kPage;
@@ -1167,6 +1184,7 @@ void vx_destroy(vx_handle* h) {
   if (!h) return;
   cudaSetDevice(h->dev);
   if (h->stream) cudaStreamSynchronize(h->stream);
+  codec_destroy(h);
   for (auto* tab : {&h->g_step, &h->g_fm, &h->g_frame_fm, &h->g_frame_bb})
     for (auto& g : *tab)
       if (g.exec) cudaGraphExecDestroy(g.exec);
@@ -1300,8 +1318,8 @@ int vx_init_random_weights(vx_handle* h, uint64_t seed) {
   CK(cudaSetDevice(h->dev));
   for (auto& kv : h->tensors) {
     const TensorSlot& t = kv.second;
-    if (t.is_norm) {
-      k_fill_f16<<<4, 256, 0, h->stream>>>(t.dst, t.cols, 1.0f);
+    if (t.fill != 0.f) {
+      k_fill_f16<<<4, 256, 0, h->stream>>>(t.dst, t.rows * t.cols, t.fill);
       CK(cudaGetLastError());
       continue;
     }
@@ -1321,6 +1339,8 @@ int vx_init_random_weights(vx_handle* h, uint64_t seed) {
   }
   CK(cudaStreamSynchronize(h->stream));
   h->weights_ready = true;
+  int rc;
+  if (h->codec && (rc = codec_prepare(h))) return rc;
   if (h->cfg.enable_fm) return build_tp_table(h);
   return VX_OK;
 }
@@ -1401,6 +1421,8 @@ int vx_read_tensor(vx_handle* h, const char* name, uint16_t* out, size_t n) {
 int vx_mark_weights_loaded(vx_handle* h) {
   if (!h) return VX_E_INVALID;
   h->weights_ready = true;
+  int rc;
+  if (h->codec && (rc = codec_prepare(h))) return rc;
   if (h->cfg.enable_fm) return build_tp_table(h);
   return VX_OK;
 }

@@ -39,7 +39,7 @@ class VxConfig(ctypes.Structure):
                 ("fm_n_layers", ctypes.c_int32), ("fm_nfe", ctypes.c_int32), ("fm_cfg_alpha", ctypes.c_float)] + \
                [(n, ctypes.c_int32) for n in ("fm_n_acoustic", "fm_semantic_vocab", "acoustic_levels", "audio_vocab",
                                                "max_seq_len", "max_slots", "max_frames", "max_voice_rows",
-                                               "enable_fm", "device", "tp_size", "tp_rank")]
+                                               "enable_fm", "device", "tp_size", "tp_rank", "enable_codec")]
 
 
 class VoxtralError(RuntimeError):
@@ -91,6 +91,9 @@ def load_library():
         "vx_backbone_step": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f32p, _f32p, _i32p]),
         "vx_backbone_step_codes": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_uint32, _u32p, _f32p]),
         "vx_fm_step": (ctypes.c_int, [H, ctypes.c_int32, _f32p, _f32p, _u32p, _u32p, _f32p]),
+        "vx_codec_decode": (ctypes.c_int, [H, _u32p, _u32p, ctypes.c_int32, _f32p]),
+        "vx_codec_debug_size": (ctypes.c_size_t, [ctypes.c_int32]),
+        "vx_codec_debug": (ctypes.c_int, [H, _u32p, _u32p, ctypes.c_int32, _f32p, ctypes.c_size_t]),
         "vx_debug_layers": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, _f32p]),
         "vx_decode": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
         "vx_decode_batch": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
@@ -168,6 +171,7 @@ class VoxtralEngine:
         self._cfg.max_frames = int(o.get("maxFrames", 2048))
         self._cfg.max_voice_rows = int(o.get("maxVoiceRows", 256))
         self._cfg.enable_fm = int(bool(o.get("enableFM", True)))
+        self._cfg.enable_codec = int(bool(o.get("enableCodec", True)))
         self._cfg.device = int(o.get("device", 0))
         self._cfg.tp_size = int(o.get("tpSize", 1))
         self._cfg.tp_rank = int(o.get("tpRank", 0))
@@ -231,7 +235,8 @@ class VoxtralEngine:
         """loadWeightsFromHF / loadFromSafetensors (src/engine.ts:569, src/weights.ts:491-669)
         from a local safetensors file: every tensor the engine has a slot for is copied in its
         stored dtype and converted to F16 on the GPU (BF16 and F32 with the reference's bit
-        rules).  Tensors the engine does not use (codec, tokenizer extras) are skipped.  With
+        rules).  Tensors the engine has no slot for (tokenizer extras, the codec when it is
+        disabled) are skipped.  With
         `required`, a slot the file does not provide raises, as the reference throws
         "Missing weight".  Returns the loaded names."""
         from .safetensors import DTYPES, SafetensorsFile
@@ -413,6 +418,34 @@ class VoxtralEngine:
                                               _p(ac, _u32p), _p(xf, _f32p)))
         return {"semantic_logits": lg, "acoustic_codes": ac, "x_final": xf, "semantic_code": int(sem[0])}
 
+    # ------------------------------------------------------------------ codec decoder
+    @staticmethod
+    def _codes(semanticCodes, acousticCodes):
+        sem = np.ascontiguousarray(semanticCodes, dtype=np.uint32).ravel()
+        ac = np.ascontiguousarray(acousticCodes, dtype=np.uint32).ravel()
+        if sem.size == 0 or ac.size != sem.size * 36:
+            raise ValueError(f"{sem.size} semantic codes need {sem.size * 36} acoustic codes, got {ac.size}")
+        return sem, ac
+
+    def codecDecode(self, semanticCodes, acousticCodes) -> np.ndarray:
+        """codecDecode (src/engine.ts:1402-1713): [T] semantic + [T, 36] acoustic codes ->
+        T * 1920 samples at 24 kHz (f32)."""
+        self._require_ready()
+        sem, ac = self._codes(semanticCodes, acousticCodes)
+        out = np.empty(sem.size * 1920, np.float32)
+        self._check(load_library().vx_codec_decode(self._h, _p(sem, _u32p), _p(ac, _u32p), sem.size, _p(out, _f32p)))
+        return out
+
+    def debugCodecDecode(self, semanticCodes, acousticCodes) -> dict:
+        """debugCodecDecode (src/engine.ts:1719-1975): the intermediates by the reference's names."""
+        self._require_ready()
+        sem, ac = self._codes(semanticCodes, acousticCodes)
+        T = sem.size
+        n = load_library().vx_codec_debug_size(T)
+        buf = np.empty(n, np.float32)
+        self._check(load_library().vx_codec_debug(self._h, _p(sem, _u32p), _p(ac, _u32p), T, _p(buf, _f32p), n))
+        return split_codec_debug(buf, T)
+
     def fmStepAndRead(self, slot: int = 0) -> np.ndarray:
         """fmStepAndRead (src/engine.ts:2386): the 36 acoustic codes."""
         return self.debugFMStep(None, slot)["acoustic_codes"]
@@ -499,10 +532,41 @@ class VoxtralEngine:
         t_gen = time.perf_counter()
         if onStage:
             onStage("fm", (t_gen - t_prefill) * 1e3)
+            onStage("codec")
+        # Phase 3: codec decode of all frames (src/engine.ts:2590-2601)
+        audio = np.zeros(0, np.float32)
+        if sem_codes and self._cfg.enable_codec:
+            audio = self.codecDecode(np.asarray(sem_codes, np.uint32), np.stack(ac_codes).astype(np.uint32))
+        t_codec = time.perf_counter()
+        if onStage:
+            onStage("codec", (t_codec - t_gen) * 1e3)
         return TTSResult(
-            semanticCodes=sem_codes, acousticCodes=[a.tolist() for a in ac_codes], audio=np.zeros(0, np.float32),
-            stats={"backboneMs": (t_prefill - t0) * 1e3, "fmMs": (t_gen - t_prefill) * 1e3, "codecMs": 0.0,
-                   "totalMs": (t_gen - t0) * 1e3, "framesGenerated": len(sem_codes)})
+            semanticCodes=sem_codes, acousticCodes=[a.tolist() for a in ac_codes], audio=audio,
+            stats={"backboneMs": (t_prefill - t0) * 1e3, "fmMs": (t_gen - t_prefill) * 1e3,
+                   "codecMs": (t_codec - t_gen) * 1e3, "totalMs": (t_codec - t0) * 1e3,
+                   "framesGenerated": len(sem_codes)})
+
+
+CODEC_DEBUG_ORDER = [("concat", 0, 292), ("after_input_conv", 0, 1024)] + [
+    item for s in range(4) for item in
+    [(f"after_stage{s}_transformer", s, 1024)] + ([(f"after_stage{s}_conv_up", s + 1, 1024)] if s < 3 else [])
+] + [("audio", 3, 240)]
+
+
+def split_codec_debug(buf: np.ndarray, T: int) -> dict:
+    """The concatenated intermediates of vx_codec_debug (and of the oracle) by name, each
+    [rows, channels] with rows = T * 2^stage; vq_embed / fsq_dequant are the two parts of
+    concat, after_output_conv the audio rows."""
+    out, off = {}, 0
+    for name, s, w in CODEC_DEBUG_ORDER:
+        rows = (T << s) if name != "audio" else 8 * T
+        out[name] = buf[off: off + rows * w].reshape(rows, w)
+        off += rows * w
+    assert off == buf.size, (off, buf.size)
+    out["vq_embed"] = out["concat"][:, :256]
+    out["fsq_dequant"] = out["concat"][:, 256:]
+    out["after_output_conv"] = out["audio"]
+    return out
 
 
 def header_symbols() -> list:
