@@ -63,6 +63,7 @@ def parse():
     ap.add_argument("--c5-slots", type=int, default=16, help="utterances of the long-context (C5) run")
     ap.add_argument("--c5-context", type=int, default=32768, help="synthetic K/V positions per utterance (C5)")
     ap.add_argument("--c5-frames", type=int, default=256, help="frames of the long-context (C5) run; 0 = skip")
+    ap.add_argument("--codec-frames", type=int, default=500, help="frames of the codec-decoder run; 0 = skip")
     return ap.parse_args()
 
 
@@ -284,6 +285,58 @@ def run_c5(args, vx, local, stream):
                          "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak_kind": kind}}
 
 
+# Codec decoder FLOPs per frame (2 per weight per token): input conv 1024 x 292 x 3, 8
+# layers over 30 token-layers per frame (stage s has 2^s tokens per frame, 2 layers)
+# of 16.8 M weights, transposed convs (14 outputs per frame x 2 taps x 1024 x 1024),
+# output conv (8 outputs per frame x 240 x 7168).
+CODEC_FLOP_PER_FRAME = 2 * (1024 * 876 + 30 * 16777216 + 14 * 2 * 1024 * 1024 + 8 * 240 * 7168)
+
+
+def measured_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def run_codec(args, vx, local, stream):
+    """codecDecode of one utterance of T frames (T * 1920 samples at 24 kHz), codes
+    copied in and the waveform copied out inside the timed region."""
+    import torch
+    T = args.codec_frames
+    eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 1}}, "maxSeqLen": 64, "maxFrames": 8,
+                            "enableFM": False, "device": local, "maxVoiceRows": 1})
+    eng.init()
+    eng.loadRandomWeights(0)
+    eng.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(7)
+    sem = rng.integers(2, 8194, T).astype(np.uint32)
+    ac = rng.integers(2, 23, (T, 36)).astype(np.uint32)
+    for _ in range(3):
+        eng.codecDecode(sem, ac)
+    ts = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        audio = eng.codecDecode(sem, ac)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    eng.destroy()
+    ms = float(np.median(ts))
+    flop = CODEC_FLOP_PER_FRAME * T
+    peak, kind = measured_tflops()
+    return {"workload": f"codec decoder: {T} frames -> {audio.size} samples ({audio.size / 24000:.1f} s at 24 kHz), "
+                        "every projection and convolution a tcgen05 GEMM with hi/lo f16 activations",
+            "ms": ms, "frames_per_s": T / (ms / 1e3), "realtime_factor": (audio.size / 24000) / (ms / 1e3),
+            "roofline": {"bound": "tensor", "algorithmic_flop": flop, "achieved": flop / (ms / 1e3) / 1e12,
+                         "peak": peak, "unit": "TFLOP/s", "frac": flop / (ms / 1e3) / 1e12 / peak, "peak_kind": kind,
+                         "note": "two MMAs per K step (hi/lo activation halves), so the tensor pipe does 2x the "
+                                 "algorithmic FLOPs"}}
+
+
 def run_b200(args):
     import torch
 
@@ -415,6 +468,10 @@ def run_b200(args):
     if args.c4_frames > 0 and tp == 1:
         c4 = run_c4(args, vx, synth, local, stream)
 
+    codec = None
+    if args.codec_frames > 0 and tp == 1 and rank == 0:
+        codec = run_codec(args, vx, local, stream)
+
     c5 = None
     if args.c5_frames > 0 and tp == 1:
         c5 = run_c5(args, vx, local, stream)
@@ -471,6 +528,7 @@ def run_b200(args):
             "prefill": prefill,
             "c4_batched": c4,
             "c5_long_context": c5,
+            "codec": codec,
             "host_enqueue_ms_per_step": host_enqueue_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
