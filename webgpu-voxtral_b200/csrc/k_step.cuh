@@ -98,6 +98,7 @@ struct StepParams {
   unsigned long long* trace;  // nullable: [G][kTraceFrames * phases][3] globaltimer stamps
   int prefetch_ahead;     // weight tiles prefetched into L2 ahead of the ring (0..kMaxPrefetchAhead)
   int prestage_kv;        // stage the first K/V page pair of each attention item during QKV
+  int prefetch_kv;        // prefetch the K/V pages of this CTA's attention items into L2 during QKV
   int n_frames;
   int mode0, token0;      // embedding of the first step
   int mode_next;          // embedding of later steps
@@ -629,6 +630,27 @@ __device__ __forceinline__ bool prestage(const StepParams& p, const CUtensorMap*
   return true;
 }
 
+// Called at the start of the QKV phase: L2 prefetch of the K/V pages of this CTA's
+// attention items, so that the attention phase's TMA loads hit L2.  The current
+// position's row is written later in the QKV phase; L2 stays coherent with that write.
+template <int N>
+__device__ __forceinline__ void prefetch_kv(const StepParams& p, int layer, int pos, int c, int G, int ctid) {
+  if (!p.prefetch_kv || ctid != 0) return;
+  int npages, pps, n_used;
+  split_plan(p, pos, npages, pps, n_used);
+  const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
+  for (int item = c; item < Tp<N>::NKV * p.n_splits; item += G) {
+    const int kvh = item / p.n_splits, split = item % p.n_splits;
+    if (split >= n_used) continue;
+    const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
+    for (int pg = pg0; pg < pg1; ++pg) {
+      const int phys = ptab[pg];
+      prefetch_l2(p.kv.pool + gemv::kv_row(p.kv, phys, layer, 0, kvh, 0) * HD, 64u * HD * 2u);
+      prefetch_l2(p.kv.pool + gemv::kv_row(p.kv, phys, layer, 1, kvh, 0) * HD, 64u * HD * 2u);
+    }
+  }
+}
+
 // Control flow is uniform across the 256 consumer threads (every named barrier is
 // reached by all of them); after a device error the work is skipped, not the barriers.
 template <int N>
@@ -1036,6 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       grid_wait<N>(p, phase * G, ctid, ar_qkv);
       trace_mark(p, c, f, kl, 0, L, ctid);
       const bool staged = prestage<N>(p, &kvmap, s, l, pos, c, ctid, a_pending);
+      prefetch_kv<N>(p, l, pos, c, G, ctid);
       {
         const ArIn a = ar_qkv ? ar_in(k_prev) : ArIn{};
         consume<6, 3, true, kTgQKV, kCW, N>(p, s, it, rit, hb[0], W.attn_norm, D, TD::TQKV, o0, c, G, cw, lane, pos, f,

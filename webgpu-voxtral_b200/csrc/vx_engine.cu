@@ -167,6 +167,7 @@ struct vx_handle {
   unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
   int prefetch_ahead = 4;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD; measured best)
   int prestage_kv = 0;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV=1; measured slower)
+  int prefetch_kv = 1;      // persistent kernel: L2 prefetch of the attention items' K/V pages during QKV (VX_PREFETCH_KV; measured -0.3 %)
   bool trace_armed = false;
 
   // token batches on the tensor cores (k_gemm.cuh): batched prefill
@@ -175,6 +176,8 @@ struct vx_handle {
   int tb_cap = 0;                      // rows per batch
   struct TbLayerMaps { CUtensorMap wqkv, wo, w13, w2; };
   std::vector<TbLayerMaps> tb_wmaps;   // per backbone layer
+  std::vector<TbLayerMaps> fm_wmaps;   // per acoustic-transformer layer (fm_tc)
+  bool fm_tc = false;                  // acoustic transformer on the tensor-core GEMM (VX_FM_GEMV=1: per-op GEMVs)
   CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl (128-row boxes)
   CUtensorMap tb_xhi64[3], tb_xlo64[3];  // the same with 64-row boxes (batches of <= 64 rows)
   std::unordered_map<long long, G> g_batch;   // batched decode step graphs, key (slot0, n)
@@ -290,6 +293,7 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
   sp.trace = h->trace_armed ? h->d_trace : nullptr;
   sp.prefetch_ahead = h->prefetch_ahead;
   sp.prestage_kv = h->prestage_kv;
+  sp.prefetch_kv = h->prefetch_kv;
   h->trace_armed = false;
   sp.n_frames = n_frames; sp.mode0 = mode0; sp.token0 = token0; sp.mode_next = mode_next;
   sp.inc_frame = inc_frame ? 1 : 0; sp.record = record ? 1 : 0;
@@ -529,6 +533,8 @@ FmParams fm_params(vx_handle* h, int slot) {
   return f;
 }
 
+int enqueue_fm_layers_tc(vx_handle* h, const FmParams& f);
+
 // fmForward for one slot on its normed state (the FM is not sharded under TP:
 // every rank computes it redundantly).
 int enqueue_fm(vx_handle* h, int slot) {
@@ -547,6 +553,9 @@ int enqueue_fm(vx_handle* h, int slot) {
   for (int s = 0; s < steps; ++s) {
     f.step = s;
     CK(launch(h, k_fm_assemble, dim3((D + 255) / 256), dim3(256), 0, f));
+    if (h->fm_tc) {
+      if ((rc = enqueue_fm_layers_tc(h, f))) return rc;
+    } else
     for (int l = 0; l < h->cfg.fm_n_layers; ++l) {
       const LayerW& W = h->fm_layers[l];
       {
@@ -711,6 +720,36 @@ int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float
   CK(launch(h, tc::k_tb_row, dim3(n), dim3(M / 12), 0, rp));
   return VX_OK;
 }
+
+// The 3 acoustic-transformer layers of one Euler step (fmTransformerPass, src/engine.ts:1057-1225)
+// on the tensor cores: the 6 sequence rows (3 positions x cond/uncond) are a token batch
+// of 6 through tcgen05 GEMMs (64-row tiles), with the pre-norms, residual adds and split-K
+// sums in k_tb_row, SwiGLU in k_tb_swiglu_split and the 3-token attention in k_fm_attn3.
+int enqueue_fm_layers_tc(vx_handle* h, const FmParams& f) {
+  const int D = h->D, F = h->cfg.hidden_dim, n = 6;
+  int rc, sp = 0;
+  if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 1, 64, f.seq, D, D, h->fm_layers[0].attn_norm, nullptr))) return rc;
+  for (int l = 0; l < h->FL; ++l) {
+    const LayerW& W = h->fm_layers[l];
+    const vx_handle::TbLayerMaps& m = h->fm_wmaps[l];
+    if ((rc = run_tc_gemm<64>(h, m.wqkv, h->tb_xhi64[0], h->tb_xlo64[0], const_cast<float*>(f.qkv), 6144, 6144, n, D, 0)))
+      return rc;
+    CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, f));
+    CK(launch(h, tc::k_tb_split, dim3(h->num_sms), dim3(256), 0, (const float*)f.att, (long long)n * 4096, h->tb_hi,
+              h->tb_lo));
+    if ((rc = run_tc_gemm<64>(h, m.wo, h->tb_xhi64[1], h->tb_xlo64[1], f.seq, D, D, n, 4096, 1, 8, &sp))) return rc;
+    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 64, f.seq, D, D, W.ffn_norm, nullptr))) return rc;
+    if ((rc = run_tc_gemm<64>(h, m.w13, h->tb_xhi64[0], h->tb_xlo64[0], h->tb_y, 2 * F, 2 * F, n, D, 0))) return rc;
+    const long long ng = (long long)n * F;
+    CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
+              dim3(256), 0, (const float*)h->tb_y, n, F, h->tb_hi, h->tb_lo));
+    if ((rc = run_tc_gemm<64>(h, m.w2, h->tb_xhi64[2], h->tb_xlo64[2], f.seq, D, D, n, F, 1, 8, &sp))) return rc;
+    const __half* next = l + 1 < h->FL ? h->fm_layers[l + 1].attn_norm : nullptr;
+    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 64, f.seq, D, D, next, nullptr))) return rc;
+  }
+  return VX_OK;
+}
+
 
 // The L layers for a batch of n activation rows in tb_h (rows described by `tr`):
 // on entry tb_hi/tb_lo must hold RMSNorm(tb_h) * attention_norm of layer 0; on
@@ -885,6 +924,17 @@ int setup_tb(vx_handle* h) {
     if ((rc = encode_f16_2d(h, &m.wo, W.wo, h->QD, D, h->QD * 2, tc::kBK, tc::kBM))) return rc;
     if ((rc = encode_f16_2d(h, &m.w13, W.w13, D, 2LL * h->Fl, D * 2, tc::kBK, tc::kBM))) return rc;
     if ((rc = encode_f16_2d(h, &m.w2, W.w2, h->Fl, D, (long long)h->Fl * 2, tc::kBK, tc::kBM))) return rc;
+  }
+  // acoustic transformer (full, unsharded weights: this path runs at tp 1 only)
+  h->fm_wmaps.resize(h->FL);
+  for (int l = 0; l < h->FL; ++l) {
+    const LayerW& W = h->fm_layers[l];
+    vx_handle::TbLayerMaps& m = h->fm_wmaps[l];
+    const long long F = h->cfg.hidden_dim;
+    if ((rc = encode_f16_2d(h, &m.wqkv, W.wqkv, D, 6144, D * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.wo, W.wo, 4096, D, 4096 * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.w13, W.w13, D, 2 * F, D * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.w2, W.w2, F, D, F * 2, tc::kBK, tc::kBM))) return rc;
   }
   return VX_OK;
 }
@@ -1164,6 +1214,7 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->dev);
     if (const char* pa = getenv("VX_PREFETCH_AHEAD")) h->prefetch_ahead = std::max(0, std::min(mk::kMaxPrefetchAhead, atoi(pa)));
     if (const char* ps = getenv("VX_PRESTAGE_KV")) h->prestage_kv = atoi(ps) != 0;
+    if (const char* pk = getenv("VX_PREFETCH_KV")) h->prefetch_kv = atoi(pk) != 0;
     const char* e = getenv("VX_NO_MEGAKERNEL");
     h->coop = coop != 0 && !(e && e[0] == '1');
     h->use_mk = h->coop && h->tp == 1;   // TP: enabled by vx_tp_p2p_open
@@ -1175,6 +1226,8 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     const char* tw = getenv("VX_PREFILL_TOKENWISE");
     h->prefill_tokenwise = tw && tw[0] == '1';
     if (h->use_tb && (rc = setup_tb(h))) { *out = h; return rc; }
+    const char* fg = getenv("VX_FM_GEMV");
+    h->fm_tc = h->use_tb && c.enable_fm && !(fg && fg[0] == '1');
   }
   *out = h;
   return VX_OK;
