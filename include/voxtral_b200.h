@@ -231,7 +231,7 @@ int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t*
  * tokens shares a layer (batched prefill; the reference prefills token by token,
  * src/engine.ts:2457-2472).  No counterpart in the reference.  Computes Y = X W^T,
  * then Y += X W^T, for seeded random W f16 [M,K] ~ N(0, 0.02) and X f32 [N,K] ~ N(0,1),
- * with tile width bn (64, 128 or 256) and at most max_splits K splits, and compares
+ * with tile width bn (16, 64, 128 or 256) and at most max_splits K splits, and compares
  * each pass with an f32 CUDA-core product of the same operands:
  * out_rel_err[2] = max|Y - Yref| / max|Yref| of the two passes. */
 int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, int32_t max_splits, uint64_t seed,

@@ -32,6 +32,9 @@ def eng(vx):
     (3072, 77, 9216, 128, 8),      # down projection, split-K
     (256, 64, 4096, 64, 4),        # narrow tile, split-K
     (512, 300, 1024, 256, 2),      # wide tile, two token tiles (second ragged)
+    (6144, 6, 3072, 16, 3),        # the acoustic transformer's 6 rows, QKV shape
+    (3072, 6, 9216, 16, 8),        # its down projection, split-K
+    (384, 40, 1024, 16, 1),        # 16-row tiles over a ragged 40-row batch
 ])
 def test_tc_gemm_selftest(eng, M, N, K, bn, splits):
     e_store, e_acc = eng.selftest_gemm(M, N, K, bn=bn, max_splits=splits, seed=M + N + K)

@@ -41,11 +41,12 @@ constexpr int kThreads = 128;
 
 template <int BN>
 struct Cfg {
-  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(BN == 16 || BN == 64 || BN == 128 || BN == 256, "BN");
   static constexpr int kA = kBM * kBK * 2;                   // 16 KB
   static constexpr int kB = BN * kBK * 2;                    // per hi / lo operand
   static constexpr int kStage = kA + 2 * kB;
-  static constexpr int kStages = (196 * 1024) / kStage;       // BN=64: 6, 128: 4, 256: 2
+  static constexpr int kStages = (196 * 1024) / kStage;       // BN=16: 9, 64: 6, 128: 4, 256: 2
+  static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;    // TMEM allocations are powers of 2 >= 32
   static constexpr size_t kSmem = (size_t)kStages * kStage + 1024 /*align*/ + 256 /*barriers*/;
   // instruction descriptor (kind::f16): D f32 (bit 4), A = B = f16, both K-major,
   // N >> 3 at bit 17, M >> 4 at bit 24
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
     prefetch_tmap(&xhi_map);
     prefetch_tmap(&xlo_map);
   }
-  if (warp == 2) tmem_alloc(tmem_slot, BN);
+  if (warp == 2) tmem_alloc(tmem_slot, C::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -220,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 

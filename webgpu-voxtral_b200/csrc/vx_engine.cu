@@ -180,6 +180,7 @@ struct vx_handle {
   bool fm_tc = false;                  // acoustic transformer on the tensor-core GEMM (VX_FM_GEMV=1: per-op GEMVs)
   CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl (128-row boxes)
   CUtensorMap tb_xhi64[3], tb_xlo64[3];  // the same with 64-row boxes (batches of <= 64 rows)
+  CUtensorMap tb_xhi16[3], tb_xlo16[3];  // and 16-row boxes (the acoustic transformer's 6 rows)
   std::unordered_map<long long, G> g_batch;   // batched decode step graphs, key (slot0, n)
   void* tb_buf = nullptr;
   float *tb_h = nullptr, *tb_y = nullptr, *tb_q = nullptr, *tb_att = nullptr, *tb_part = nullptr, *tb_ws = nullptr;
@@ -261,7 +262,7 @@ int prime_kernel_attrs(vx_handle* h) {
   CK(cudaFuncSetAttribute(mk::k_decode_steps<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
   CK(cudaFuncSetAttribute(k_fm_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem));
   CK(cudaFuncSetAttribute(k_top_p_test, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem));
-  CK(tc_attr<64>()); CK(tc_attr<128>()); CK(tc_attr<256>());
+  CK(tc_attr<16>()); CK(tc_attr<64>()); CK(tc_attr<128>()); CK(tc_attr<256>());
   return VX_OK;
 }
 
@@ -723,29 +724,29 @@ int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float
 
 // The 3 acoustic-transformer layers of one Euler step (fmTransformerPass, src/engine.ts:1057-1225)
 // on the tensor cores: the 6 sequence rows (3 positions x cond/uncond) are a token batch
-// of 6 through tcgen05 GEMMs (64-row tiles), with the pre-norms, residual adds and split-K
+// of 6 through tcgen05 GEMMs (16-row tiles, 9-stage weight pipeline), with the pre-norms, residual adds and split-K
 // sums in k_tb_row, SwiGLU in k_tb_swiglu_split and the 3-token attention in k_fm_attn3.
 int enqueue_fm_layers_tc(vx_handle* h, const FmParams& f) {
   const int D = h->D, F = h->cfg.hidden_dim, n = 6;
   int rc, sp = 0;
-  if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 1, 64, f.seq, D, D, h->fm_layers[0].attn_norm, nullptr))) return rc;
+  if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 1, 16, f.seq, D, D, h->fm_layers[0].attn_norm, nullptr))) return rc;
   for (int l = 0; l < h->FL; ++l) {
     const LayerW& W = h->fm_layers[l];
     const vx_handle::TbLayerMaps& m = h->fm_wmaps[l];
-    if ((rc = run_tc_gemm<64>(h, m.wqkv, h->tb_xhi64[0], h->tb_xlo64[0], const_cast<float*>(f.qkv), 6144, 6144, n, D, 0)))
+    if ((rc = run_tc_gemm<16>(h, m.wqkv, h->tb_xhi16[0], h->tb_xlo16[0], const_cast<float*>(f.qkv), 6144, 6144, n, D, 0)))
       return rc;
     CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, f));
     CK(launch(h, tc::k_tb_split, dim3(h->num_sms), dim3(256), 0, (const float*)f.att, (long long)n * 4096, h->tb_hi,
               h->tb_lo));
-    if ((rc = run_tc_gemm<64>(h, m.wo, h->tb_xhi64[1], h->tb_xlo64[1], f.seq, D, D, n, 4096, 1, 8, &sp))) return rc;
-    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 64, f.seq, D, D, W.ffn_norm, nullptr))) return rc;
-    if ((rc = run_tc_gemm<64>(h, m.w13, h->tb_xhi64[0], h->tb_xlo64[0], h->tb_y, 2 * F, 2 * F, n, D, 0))) return rc;
+    if ((rc = run_tc_gemm<16>(h, m.wo, h->tb_xhi16[1], h->tb_xlo16[1], f.seq, D, D, n, 4096, 1, 8, &sp))) return rc;
+    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, W.ffn_norm, nullptr))) return rc;
+    if ((rc = run_tc_gemm<16>(h, m.w13, h->tb_xhi16[0], h->tb_xlo16[0], h->tb_y, 2 * F, 2 * F, n, D, 0))) return rc;
     const long long ng = (long long)n * F;
     CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
               dim3(256), 0, (const float*)h->tb_y, n, F, h->tb_hi, h->tb_lo));
-    if ((rc = run_tc_gemm<64>(h, m.w2, h->tb_xhi64[2], h->tb_xlo64[2], f.seq, D, D, n, F, 1, 8, &sp))) return rc;
+    if ((rc = run_tc_gemm<16>(h, m.w2, h->tb_xhi16[2], h->tb_xlo16[2], f.seq, D, D, n, F, 1, 8, &sp))) return rc;
     const __half* next = l + 1 < h->FL ? h->fm_layers[l + 1].attn_norm : nullptr;
-    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 64, f.seq, D, D, next, nullptr))) return rc;
+    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, next, nullptr))) return rc;
   }
   return VX_OK;
 }
@@ -915,6 +916,8 @@ int setup_tb(vx_handle* h) {
     if ((rc = encode_f16_2d(h, &h->tb_xlo[i], h->tb_lo, ks[i], cap, ks[i] * 2, tc::kBK, 128))) return rc;
     if ((rc = encode_f16_2d(h, &h->tb_xhi64[i], h->tb_hi, ks[i], cap, ks[i] * 2, tc::kBK, 64))) return rc;
     if ((rc = encode_f16_2d(h, &h->tb_xlo64[i], h->tb_lo, ks[i], cap, ks[i] * 2, tc::kBK, 64))) return rc;
+    if ((rc = encode_f16_2d(h, &h->tb_xhi16[i], h->tb_hi, ks[i], cap, ks[i] * 2, tc::kBK, 16))) return rc;
+    if ((rc = encode_f16_2d(h, &h->tb_xlo16[i], h->tb_lo, ks[i], cap, ks[i] * 2, tc::kBK, 16))) return rc;
   }
   h->tb_wmaps.resize(h->L);
   for (int l = 0; l < h->L; ++l) {
@@ -1265,7 +1268,7 @@ int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, 
                      double* out_rel_err) {
   if (!h || !out_rel_err) return VX_E_INVALID;
   if (!h->use_tb) return h->fail(VX_E_STATE, "token-batch path is off (tp > 1 or VX_NO_BATCHED_PREFILL)");
-  if (M < 1 || N < 1 || K < 64 || K % 64 || !(bn == 64 || bn == 128 || bn == 256) || max_splits < 1 ||
+  if (M < 1 || N < 1 || K < 64 || K % 64 || !(bn == 16 || bn == 64 || bn == 128 || bn == 256) || max_splits < 1 ||
       (long long)M * K > (1LL << 28) || (long long)N * K > (1LL << 26) || (long long)N * M > (1LL << 26))
     return h->fail(VX_E_INVALID, "selftest shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
   CK(cudaSetDevice(h->dev));
@@ -1291,7 +1294,8 @@ int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, 
       rc = h->fail(VX_E_CUDA, "selftest fill");
   }
   for (int pass = 0; pass < 2 && !rc; ++pass) {
-    if (bn == 64) rc = run_tc_gemm<64>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
+    if (bn == 16) rc = run_tc_gemm<16>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
+    else if (bn == 64) rc = run_tc_gemm<64>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
     else if (bn == 128) rc = run_tc_gemm<128>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
     else rc = run_tc_gemm<256>(h, wm, xh, xl, Y, M, M, N, K, pass, max_splits);
     if (!rc && pass == 0) {
