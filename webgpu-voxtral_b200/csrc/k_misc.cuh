@@ -366,6 +366,8 @@ struct FmParams {
   float* seq;                // [6][D]: cond (x_proj, t_proj, llm), uncond (x_proj, t_proj, 0)
   const float* qkv;          // [6][q+2kv]
   float* att;                // [6][q]
+  __half* att_hi;            // non-null: the attention rows go out as the f16 hi/lo operand
+  __half* att_lo;            //   of the o_proj tensor-core GEMM instead of f32 [6][q]
   int q_dim, kv_dim, n_heads, n_kv;
   const float* vel;          // [2][36] (cond, uncond)
   float alpha, dt;
@@ -872,8 +874,17 @@ __global__ void __launch_bounds__(128) k_fm_attn3(const __grid_constant__ FmPara
     float sum = 0.f;
     for (int j = 0; j < 3; ++j) { sc[qi][j] = expf(sc[qi][j] - mx); sum += sc[qi][j]; }
     for (int j = 0; j < 3; ++j) sc[qi][j] /= sum;
-    float* o = p.att + (3LL * seq + qi) * p.q_dim + h * 128 + lane * 4;
-    for (int e = 0; e < 4; ++e) o[e] = sc[qi][0] * v[0][e] + sc[qi][1] * v[1][e] + sc[qi][2] * v[2][e];
+    const long long o = (3LL * seq + qi) * p.q_dim + h * 128 + lane * 4;
+    for (int e = 0; e < 4; ++e) {
+      const float a = sc[qi][0] * v[0][e] + sc[qi][1] * v[1][e] + sc[qi][2] * v[2][e];
+      if (p.att_hi) {
+        const __half hv = __float2half_rn(a);
+        p.att_hi[o + e] = hv;
+        p.att_lo[o + e] = __float2half_rn(a - __half2float(hv));
+      } else {
+        p.att[o + e] = a;
+      }
+    }
   }
 }
 

@@ -735,9 +735,10 @@ int enqueue_fm_layers_tc(vx_handle* h, const FmParams& f) {
     const vx_handle::TbLayerMaps& m = h->fm_wmaps[l];
     if ((rc = run_tc_gemm<16>(h, m.wqkv, h->tb_xhi16[0], h->tb_xlo16[0], const_cast<float*>(f.qkv), 6144, 6144, n, D, 0)))
       return rc;
-    CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, f));
-    CK(launch(h, tc::k_tb_split, dim3(h->num_sms), dim3(256), 0, (const float*)f.att, (long long)n * 4096, h->tb_hi,
-              h->tb_lo));
+    FmParams fa = f;   // attention output straight into the o_proj operand
+    fa.att_hi = h->tb_hi;
+    fa.att_lo = h->tb_lo;
+    CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, fa));
     if ((rc = run_tc_gemm<16>(h, m.wo, h->tb_xhi16[1], h->tb_xlo16[1], f.seq, D, D, n, 4096, 1, 8, &sp))) return rc;
     if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, W.ffn_norm, nullptr))) return rc;
     if ((rc = run_tc_gemm<16>(h, m.w13, h->tb_xhi16[0], h->tb_xlo16[0], h->tb_y, 2 * F, 2 * F, n, D, 0))) return rc;
