@@ -74,3 +74,14 @@ def test_codebook_normalisation_uses_usage():
             assert np.array_equal(d["concat"][i, :256], row)
     finally:
         c.close()
+
+
+def test_debug_layout_matches_engine(vx):
+    """The engine's vx_codec_debug buffer and the oracle's use the same layout."""
+    eng_mod = __import__("importlib").import_module("webgpu-voxtral_b200.engine")
+    assert [n for n, _, _ in eng_mod.CODEC_DEBUG_ORDER] == [n for n, _, _ in oracle.CODEC_ORDER]
+    T = 3
+    n = vx.load_library().vx_codec_debug_size(T)
+    assert n == oracle.lib().orc_codec_debug_size(T)
+    parts = eng_mod.split_codec_debug(np.zeros(n, np.float32), T)
+    assert parts["audio"].shape == (8 * T, 240) and parts["after_stage2_conv_up"].shape == (8 * T, 1024)

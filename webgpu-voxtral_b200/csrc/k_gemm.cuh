@@ -331,18 +331,22 @@ struct RowParams {
   __half *hi, *lo;           // [N][M]
   RopeKvParams rope;         // kRowQkv (rope.qkv unused)
 };
-// Launched with M / 12 threads per row: each thread owns 3 float4 groups and issues
-// the loads of every split at once (up to kMaxRowSplits in flight).
+// Launched with M / 4, M / 8 or M / 12 threads per row (a multiple of 32, at most
+// 1024): each thread owns 1-3 float4 groups and issues the loads of every split at
+// once (up to kMaxRowSplits in flight).
 constexpr int kMaxRowSplits = 8;
-__global__ void __launch_bounds__(512) k_tb_row(const __grid_constant__ RowParams p) {
+__global__ void __launch_bounds__(1024) k_tb_row(const __grid_constant__ RowParams p) {
   griddep_launch();
   griddep_wait();
-  __shared__ float sh[16];
+  __shared__ float sh[32];
   const int n = blockIdx.x;
   const int nt = blockDim.x;
+  const int G = p.M / (4 * nt);   // float4 groups per thread
   float4 v[3];
 #pragma unroll
   for (int u = 0; u < 3; ++u) {
+    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (u >= G) continue;
     const int m = (threadIdx.x + nt * u) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.splits == 0) {
@@ -369,7 +373,8 @@ __global__ void __launch_bounds__(512) k_tb_row(const __grid_constant__ RowParam
     if (!p.norm_w) return;
     float ss = 0.f;
 #pragma unroll
-    for (int u = 0; u < 3; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+    for (int u = 0; u < 3; ++u)
+      if (u < G) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
     __syncthreads();
@@ -378,6 +383,7 @@ __global__ void __launch_bounds__(512) k_tb_row(const __grid_constant__ RowParam
     const float rms = 1.0f / sqrtf(tot / (float)p.M + p.eps);
 #pragma unroll
     for (int u = 0; u < 3; ++u) {
+      if (u >= G) continue;
       const int m = (threadIdx.x + nt * u) * 4;
       const __half2* w2 = reinterpret_cast<const __half2*>(p.norm_w + m);
       const float2 wa = __half22float2(w2[0]), wb = __half22float2(w2[1]);
@@ -398,6 +404,7 @@ __global__ void __launch_bounds__(512) k_tb_row(const __grid_constant__ RowParam
   const int page = page_ok ? r.page_table[(long long)slot * r.max_pages + lp] : 0;
 #pragma unroll
   for (int u = 0; u < 3; ++u) {
+    if (u >= G) continue;
     const int m = (threadIdx.x + nt * u) * 4;
     float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
     if (m < r.q_dim + r.kv_dim) {

@@ -165,7 +165,7 @@ struct vx_handle {
   mk::LayerPtrs* d_layers = nullptr;
   unsigned* d_bar = nullptr;
   unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
-  int prefetch_ahead = 4;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD; measured best)
+  int prefetch_ahead = 3;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD; measured best)
   int prestage_kv = 0;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV=1; measured slower)
   int prefetch_kv = 1;      // persistent kernel: L2 prefetch of the attention items' K/V pages during QKV (VX_PREFETCH_KV; measured -0.3 %)
   bool trace_armed = false;
@@ -716,9 +716,13 @@ int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float
   rp.ws = h->tb_ws; rp.splits = splits; rp.n_tiles = n_tiles; rp.bn = bn; rp.y = y; rp.ldy = ldy; rp.M = M;
   rp.mode = mode; rp.norm_w = norm_w; rp.eps = h->cfg.norm_eps; rp.hi = h->tb_hi; rp.lo = h->tb_lo;
   if (rope) rp.rope = *rope;
-  if (M % 12 || M / 12 > 512 || (M / 12) % 32) return h->fail(VX_E_INVALID, "row width %d", M);
+  // threads per row: as many as the row allows (one float4 group each), for latency
+  int nt = 0;
+  for (int g = 1; g <= 3 && !nt; ++g)
+    if (M % (4 * g) == 0 && M / (4 * g) <= 1024 && (M / (4 * g)) % 32 == 0) nt = M / (4 * g);
+  if (!nt) return h->fail(VX_E_INVALID, "row width %d", M);
   if (splits > tc::kMaxRowSplits) return h->fail(VX_E_INVALID, "%d split-K partials per row", splits);
-  CK(launch(h, tc::k_tb_row, dim3(n), dim3(M / 12), 0, rp));
+  CK(launch(h, tc::k_tb_row, dim3(n), dim3(nt), 0, rp));
   return VX_OK;
 }
 
