@@ -138,8 +138,9 @@ int vx_backbone_step_codes(vx_handle* h, int32_t slot, uint32_t semantic_code, c
 /* fmForward (src/engine.ts:1240-1380) on the slot's current normed state, as
  * exposed by debugFMStep(noise) / fmStepAndRead (:2363-2398).  noise [36]
  * (nullable: the slot's seeded stream).  Outputs (all nullable): semantic logits
- * [semantic_vocab], the masked-argmax semantic code (index 0 and >= 8194 masked,
- * :2559-2563), acoustic codes [36], x_final [36]. */
+ * [semantic_vocab], the semantic code chosen from them (index 0 and >= 8194 masked,
+ * :2559-2563; masked argmax, or top-p sampling when vx_set_sampling enabled it), acoustic
+ * codes [36], x_final [36]. */
 int vx_fm_step(vx_handle* h, int32_t slot, const float* noise, float* semantic_logits, uint32_t* semantic_code,
                uint32_t* acoustic_codes, float* x_final);
 
@@ -152,8 +153,9 @@ int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out);
 /* Device-resident frame loop of generate() (src/engine.ts:2498-2585) with the
  * host round trips removed: n_frames frames starting at the slot's current frame,
  * each one CUDA graph.  with_fm = 1: frame f > 0 embeds frame f-1's codes, runs the
- * backbone, then fmForward with the slot's noise stream and masked argmax (frame
- * 0 runs the FM on the state left by the AUDIO kick).  with_fm = 0 (backbone-only):
+ * backbone, then fmForward with the slot's noise stream and the slot's semantic
+ * selection (masked argmax or top-p, vx_set_sampling; frame 0 runs the FM on the state
+ * left by the AUDIO kick).  with_fm = 0 (backbone-only):
  * frame 0 is the AUDIO kick (token 24, text embedding, :2481-2487) and frame f > 0
  * embeds the synthetic codes of frame f-1.  Asynchronous: returns after enqueueing;
  * read results with vx_read_codes / vx_read_normed after vx_synchronize. */

@@ -407,7 +407,8 @@ class VoxtralEngine:
         return normed
 
     def debugFMStep(self, debugNoise=None, slot: int = 0) -> dict:
-        """debugFMStep(noise) (src/engine.ts:2363) plus the masked-argmax semantic code."""
+        """debugFMStep(noise) (src/engine.ts:2363) plus the semantic code the slot selects
+        (masked argmax, or top-p after set_sampling('top_p'))."""
         self._require_ready()
         lg = np.empty(self._cfg.fm_semantic_vocab, np.float32)
         sem = np.zeros(1, np.uint32)
