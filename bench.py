@@ -8,9 +8,13 @@ batch-1 decode (frame 0 is the AUDIO kick, frames 1..499 embed the previous fram
 37 codes) from the post-prefill checkpoint.  value = frames/s of the whole job.
 
   N = 1   : one utterance on one GPU.
-  N > 1   : launched by torchrun, one process per GPU; data-parallel replicas (each
-            rank decodes its own utterance, no collective in the data path), weak
-            scaling, device time = max over ranks.
+  N > 1   : launched by torchrun, one process per GPU.  The headline is the batch-1
+            latency path: ONE utterance decoded tensor-parallel over the N GPUs (heads and
+            FFN columns sharded, two all-reduces per layer inside the persistent kernel
+            over NVLink peer memory), strong scaling, device time = max over ranks.
+            `--mode dp` instead runs N independent replicas (weak scaling).  The batched
+            throughput leg (C4) is always data-parallel: every rank decodes its own 64
+            utterances, and its frames/s is summed over ranks (time = max over ranks).
 
 `--impl reference` times the reference's algorithm on the host cores instead: the CPU
 restatement in oracle/ (the reference itself is TypeScript + WGSL and cannot run here).
@@ -53,10 +57,12 @@ def parse():
     ap.add_argument("--layers", type=int, default=26)
     ap.add_argument("--text", type=int, default=N_TEXT, help="text ids in the prompt (C2: 512)")
     ap.add_argument("--voice", type=int, default=N_VOICE, help="voice rows in the prompt (C2: 100)")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="length of the cpu_baseline sample of the GPU arm (the reference arm times --steps steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", default="dp", choices=["dp", "tp"],
-                    help="N > 1: dp = one utterance per GPU (weak scaling); tp = one utterance over N GPUs")
+    ap.add_argument("--mode", default="tp", choices=["dp", "tp"],
+                    help="N > 1: tp = one utterance over N GPUs (strong scaling, default); dp = one utterance "
+                         "per GPU (weak scaling)")
     ap.add_argument("--c3-frames", type=int, default=40, help="frames of the backbone+FM (C3) sample; 0 = skip")
     ap.add_argument("--c4-slots", type=int, default=64, help="utterances decoded in lockstep per GPU (C4)")
     ap.add_argument("--c4-frames", type=int, default=1500, help="frames of the batched (C4) run; 0 = skip")
@@ -136,11 +142,18 @@ def nccl_lib_path():
         return None
 
 
-def cpu_sample(n_layers: int, seconds: float, n_frames_min: int = 2):
-    """The CPU restatement (oracle/) on the host cores: decode frames at the C2 context length."""
+def mean_position(args) -> int:
+    """Mean KV position of a decode step: the prompt (text + voice + 5 control tokens)
+    plus half the step's frames.  The CPU legs sample frames there, so the per-frame KV
+    work matches the average frame of the GPU arm."""
+    return args.text + args.voice + 5 + (args.frames - 1) // 2
+
+
+def cpu_sample(args, seconds: float, n_frames_min: int = 2):
+    """The CPU restatement (oracle/) on the host cores: decode frames at the step's mean position."""
     import oracle
-    o = oracle.Oracle(n_layers=n_layers, max_seq=4096, with_fm=False)
-    o.fill_kv(N_TEXT + N_VOICE + 5, seed=11)
+    o = oracle.Oracle(n_layers=args.layers, max_seq=4096, with_fm=False)
+    o.fill_kv(mean_position(args), seed=11)
     rng = np.random.default_rng(0)
     emb = rng.standard_normal(3072).astype(np.float32) * 0.1
     o.backbone_step(0, embed=emb)                 # warm-up step
@@ -160,7 +173,7 @@ def run_reference(args):
         return 0
     import oracle
     o = oracle.Oracle(n_layers=args.layers, max_seq=4096, with_fm=False)
-    o.fill_kv(N_TEXT + N_VOICE + 5, seed=11)
+    o.fill_kv(mean_position(args), seed=11)
     emb = (np.random.default_rng(0).standard_normal(3072) * 0.1).astype(np.float32)
     frames_per_step = 2
     start = o.position
@@ -183,7 +196,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 weights, f32 math, f32 KV", "data": "synthetic",
         "config": {"workload": WORKLOAD, "parallelism": "host cores", "sample": "per step: 2 backbone frames at "
-                   f"position {start} (KV prefilled with synthetic values) of the {args.layers}-layer model"},
+                   f"position {start} (the mean position of a {args.frames}-frame step after a "
+                   f"{args.text + args.voice + 5}-position prompt; KV prefilled with synthetic values) of the "
+                   f"{args.layers}-layer model"},
         "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "port",
                          "sample": f"{frames_per_step} frames x {args.steps} steps at position {start}"},
         "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -193,7 +208,7 @@ def run_reference(args):
     return 0
 
 
-def run_c4(args, vx, synth, local, stream):
+def run_c4(args, vx, synth, local, stream, vdist, rank, world):
     """C4: S utterances per GPU (prompt 256 text ids + 100 voice rows each),
     decoded in lockstep for F frames with vx_decode_batch (tensor-core GEMMs over the
     slots, paged f16 KV).  Times the whole F-frame run with CUDA events (inputs resident)."""
@@ -205,11 +220,12 @@ def run_c4(args, vx, synth, local, stream):
     eng.loadRandomWeights(0)
     eng.set_stream(stream.cuda_stream)
     p0 = None
+    ub = 1000 + S * rank                      # every rank decodes its own utterances
     for u in range(S):
-        toks, a0, na = synth.prompt(1000 + u, 256, 100)
+        toks, a0, na = synth.prompt(ub + u, 256, 100)
         eng.reset(slot=u)
-        eng.set_streams(3, 4, 1000 + u, slot=u)
-        eng.prefill(toks, a0, na, synth.voice_rows(1000 + u, 100), slot=u)
+        eng.set_streams(3, 4, ub + u, slot=u)
+        eng.prefill(toks, a0, na, synth.voice_rows(ub + u, 100), slot=u)
         p0 = len(toks)
     eng.synchronize()
     for u in range(S):
@@ -218,13 +234,15 @@ def run_c4(args, vx, synth, local, stream):
     for u in range(S):
         eng.rewind(slot=u)
     torch.cuda.synchronize()
+    vdist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     l0 = eng.launch_count()
     e0.record(stream)
     eng.decode_batch(F4, S)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    vdist.barrier()
+    ms = vdist.max_over_ranks(e0.elapsed_time(e1))
     launches = eng.launch_count() - l0
     eng.destroy()
     step_ms = ms / F4
@@ -233,8 +251,10 @@ def run_c4(args, vx, synth, local, stream):
     flops = 2.0 * S * args.layers * (BYTES_PER_LAYER / 2)
     peak, kind = measured_peaks()
     return {"workload": f"C4: {S} utterances per GPU in lockstep (prompt 256 text ids + 100 voice rows = {p0} positions "
-                        f"each), {F4} frames, paged f16 KV, maxSeqLen 2048; weights streamed once per step for all slots",
-            "frames_per_s": S * F4 / (ms / 1e3), "ms_per_step": step_ms, "slots": S, "frames": F4,
+                        f"each), {F4} frames, paged f16 KV, maxSeqLen 2048; weights streamed once per step for all slots; "
+                        f"data-parallel over {world} GPU(s), frames/s summed over ranks, time = max over ranks",
+            "frames_per_s": world * S * F4 / (ms / 1e3), "frames_per_s_per_gpu": S * F4 / (ms / 1e3),
+            "parallelism": f"dp{world}", "ms_per_step": step_ms, "slots": S, "frames": F4,
             "avg_position": avg_pos, "gpu_launches": launches,
             "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
                          "achieved": step_bytes / (step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
@@ -443,7 +463,7 @@ def run_b200(args):
 
     # ------------------------------------------------------------------ C3 sample: backbone + FM per frame
     c3 = None
-    if args.c3_frames > 0 and tp == 1:
+    if args.c3_frames > 0:
         eng.rewind()
         eng.set_sampling("top_p", 0.9, 0.8, seed=1)   # generate()'s sampleTopP(semLogits, 0.9, 0.8)
         eng.backboneStep(24)                       # AUDIO kick: frame 0's hidden state
@@ -454,19 +474,19 @@ def run_b200(args):
         eng.decode(args.c3_frames, with_fm=True)
         c1.record(stream)
         torch.cuda.synchronize()
-        c3_ms = c0.elapsed_time(c1) / args.c3_frames
+        c3_ms = vdist.max_over_ranks(c0.elapsed_time(c1)) / args.c3_frames
         eng.set_sampling("argmax")
         c3 = {"frames_per_s": 1e3 / c3_ms, "ms_per_frame": c3_ms, "frames": args.c3_frames,
               "workload": "C3: one backbone step + FM (7 Euler steps, CFG as batch 2, M=6 skinny GEMMs) + "
                           "semantic code by the reference's top-p sampler (p 0.9, temperature 0.8, seeded draws) "
-                          "per frame, device-resident",
+                          f"per frame, device-resident; {'one GPU' if tp == 1 else f'tensor-parallel over {tp} GPUs'}",
               "fm_bytes_per_frame": 4961851392,
               "frame_gbs": (frame_bytes + 4961851392) / (c3_ms / 1e3) / 1e9}
 
     # ------------------------------------------------------------------ C4: batched lockstep decode
     c4 = None
-    if args.c4_frames > 0 and tp == 1:
-        c4 = run_c4(args, vx, synth, local, stream)
+    if args.c4_frames > 0:
+        c4 = run_c4(args, vx, synth, local, stream, vdist, rank, world)
 
     codec = None
     if args.codec_frames > 0 and tp == 1 and rank == 0:
@@ -494,15 +514,17 @@ def run_b200(args):
             e2e_vals.append(F / (t0.elapsed_time(t1) / 1e3))
         h2d = toks.nbytes + voice.nbytes
         d2h = codes.nbytes + normed.nbytes
-    e2e = vdist.sum_over_ranks(min(e2e_vals)) if (world > 1 and tp == 1) else e2e_vals[0]
+    # frames/s of the whole job: the slowest rank's time (TP: one utterance; DP: one per rank)
+    e2e = (world if tp == 1 else 1) * vdist.min_over_ranks(min(e2e_vals))
 
     # ------------------------------------------------------------------ CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        fps, n, dt, cores = cpu_sample(args.layers, args.cpu_seconds)
+        fps, n, dt, cores = cpu_sample(args, args.cpu_seconds)
         cpu = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
-               "sample": f"{n} backbone frames of the {args.layers}-layer model at position {N_TEXT + N_VOICE + 5} "
-                         f"(KV prefilled synthetically), {dt:.1f} s, oracle/oracle.cpp with OpenMP"}
+               "sample": f"{n} backbone frames of the {args.layers}-layer model at position {mean_position(args)} "
+                         f"(the step's mean position; KV prefilled synthetically), {dt:.1f} s, oracle/oracle.cpp "
+                         "with OpenMP"}
 
     if rank == 0:
         line = {

@@ -147,7 +147,9 @@ int vx_fm_step(vx_handle* h, int32_t slot, const float* noise, float* semantic_l
 /* debugBackboneLayerByLayer (src/engine.ts:2106-2287) at the slot's position for
  * tok_embeddings[token]: out [(4*n_layers+3)][dim] = embed, per layer {attn_norm,
  * attn_out (hidden after the attention residual), ffn_norm, ffn_out}, final_norm,
- * hidden.  Advances the position like the reference. */
+ * hidden.  Advances the position like the reference.  The step runs in the persistent
+ * decode kernel that vx_decode runs (option persistent_decode, on by default), which
+ * records these tensors as it goes; with that option off, in the per-op kernels. */
 int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out);
 
 /* Device-resident frame loop of generate() (src/engine.ts:2498-2585) with the
@@ -160,6 +162,12 @@ int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out);
  * embeds the synthetic codes of frame f-1.  Asynchronous: returns after enqueueing;
  * read results with vx_read_codes / vx_read_normed after vx_synchronize. */
 int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm);
+
+/* vx_decode(slot, n_frames, 0) that also records the per-layer tensors of frame
+ * record_frame of this call, in the layout of vx_debug_layers, into out
+ * [(4*n_layers+3)][dim] (debugBackboneLayerByLayer, src/engine.ts:2106-2287, taken inside
+ * the benchmarked frame loop instead of as a separate step).  Synchronous. */
+int vx_decode_record(vx_handle* h, int32_t slot, int32_t n_frames, int32_t record_frame, float* out);
 
 /* Batched backbone-only decode: n_frames frames of slots [slot0, slot0 + n_slots) in
  * lockstep, each slot at its own position with its own synthetic feedback codes
@@ -206,6 +214,28 @@ int vx_rewind(vx_handle* h, int32_t slot);
  * stream) for all later work; NULL restores the handle's own stream. */
 int vx_set_stream(vx_handle* h, void* stream);
 int vx_synchronize(vx_handle* h);
+
+/* Engine options.  Returns VX_E_INVALID for an unknown name or value, VX_E_STATE /
+ * VX_E_RANGE when the handle cannot take the value.  No counterpart in the reference
+ * (EngineOptions, src/engine.ts:213-219, has none of these).
+ *   "persistent_decode"  1 (default where cooperative launch exists): vx_decode,
+ *                        token-by-token vx_prefill and vx_debug_layers run the
+ *                        persistent decode kernel; 0: one CUDA graph of per-op kernels
+ *                        per step.
+ *   "batched_prefill"    1 (default, tp_size 1): vx_prefill runs the prompt through
+ *                        tensor-core GEMMs in batches of up to 512 positions; 0: token
+ *                        by token, as the reference (src/engine.ts:2457-2472).
+ *   "l2_prefetch_tiles"  0-32 (default 3): weight tiles the persistent kernel prefetches
+ *                        into L2 ahead of its shared-memory ring.
+ *   "wait_limit"         polls before a wait of the persistent kernel on a grid barrier
+ *                        or on a tensor-parallel peer's all-reduce words gives up and the
+ *                        call returns VX_E_DEVICE (0, default: 2^27 / 2^24 polls, seconds).
+ *   "tp_loopback"        1 (test support, tp_size > 1, one process): every peer receive
+ *                        buffer is this handle's own, so the other ranks' all-reduce words
+ *                        never arrive; a decode then ends in VX_E_DEVICE once wait_limit
+ *                        expires, which exercises the failure path of a lost rank without
+ *                        a second GPU. */
+int vx_set_option(vx_handle* h, const char* name, int64_t value);
 
 /* Kernel launches enqueued by this handle since creation (graph launches count
  * the kernels they contain). */
@@ -291,14 +321,17 @@ int vx_tp_p2p_open(vx_handle* h, const uint8_t* handles /* [tp_size][64] */);
  * own device buffers here.  Computes *out_index = argmax_r (W[r,:] . x) (maximum value,
  * lowest index on ties) and *out_value = that maximum (nullable), the same greedy
  * choice as vx_backbone_step's argmax_out, in one kernel that allocates nothing.
+ * A NaN product never wins; if every product is NaN, *out_index = -1 and *out_value
+ * = NaN.
  * weight: device f16 bits [rows][dim], 16-byte aligned; x: device f32 [dim];
  * out_index / out_value: device; stream: cudaStream_t (NULL = default stream);
  * err (nullable): receives a message.  Limits: rows <= 2,097,152, dim a multiple of 8
  * and <= 16,384 (VX_E_RANGE beyond them).  Its scratch is a 65,792-byte static device
  * array that every GPU loading the library holds until the process exits; the first
  * call on a device looks up that array's address (call it once before any stream
- * capture).  All calls on a device share the array, so calls that overlap on the GPU
- * race; calls ordered on one stream do not. */
+ * capture) and later calls reuse it, so the entry point must not be called on a device
+ * after cudaDeviceReset of that device.  All calls on a device share the array, so calls
+ * that overlap on the GPU race; calls ordered on one stream do not. */
 int vx_lm_head_argmax_noalloc(const uint16_t* weight, const float* x, int32_t rows, int32_t dim, int32_t* out_index,
                               float* out_value, void* stream, char* err, size_t err_len);
 

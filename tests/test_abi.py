@@ -50,3 +50,13 @@ def test_engine_without_gpu_fails_loudly(vx):
     assert not e.isReady
     with pytest.raises(vx.VoxtralError, match="not initialized"):
         e.generate([1, 2], 0, 0, None, 1)
+
+
+def test_node_binding_covers_header(vx):
+    """The committed Node binding (webgpu-voxtral_b200/node/voxtral_b200.ts, untested here:
+    no Node in this container) binds every function the header declares, with the
+    header's name."""
+    import os
+    ts = open(os.path.join(os.path.dirname(vx.library_path()), "node", "voxtral_b200.ts")).read()
+    bound = set(re.findall(r"lib\.func\('[^(']*?\b(vx_[a-z_0-9]+)\(", ts))
+    assert set(vx.header_symbols()) <= bound, set(vx.header_symbols()) - bound

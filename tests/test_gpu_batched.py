@@ -1,8 +1,6 @@
 """Tensor-core (tcgen05 / TMEM) token-batch path: the GEMM itself, and the batched
 prefill that replaces the reference's token-by-token prefill loop
 (src/engine.ts:2457-2472) against the token-by-token path and the CPU oracle."""
-import os
-
 import numpy as np
 import pytest
 
@@ -43,15 +41,11 @@ def test_tc_gemm_selftest(eng, M, N, K, bn, splits):
 
 
 def _kick_layers(vx, synth, utt, T, R, batched):
-    if not batched:
-        os.environ["VX_NO_BATCHED_PREFILL"] = "1"
+    e = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 1024, "maxFrames": 16,
+                          "enableFM": False})
+    e.init()
     try:
-        e = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": 1024, "maxFrames": 16,
-                              "enableFM": False})
-        e.init()
-    finally:
-        os.environ.pop("VX_NO_BATCHED_PREFILL", None)
-    try:
+        e.set_option("batched_prefill", 1 if batched else 0)
         e.loadRandomWeights(0)
         toks, a0, na = synth.prompt(utt, T, R)
         e.prefill(toks, a0, na, synth.voice_rows(utt, R))

@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_decode(const __grid_constant_
   if (!ok && threadIdx.x == 0) {
     // Drain any copy still in flight before the shared memory is released.
     for (int i = issued > 2 ? issued - 2 : 0; i < issued; ++i)
-      if (!mbar_wait(&full[i & 1], (uint32_t)(i >> 1) & 1u, kDevTimeoutDrain)) break;
+      if (!mbar_wait_drain(&full[i & 1], (uint32_t)(i >> 1) & 1u)) break;
   }
 
   // ---- per-warp state -> shared, merge the 4 warps, write this split's partial

@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer
+    int issued = 0;
     for (int i = 0; i < nk; ++i) {
       const int s = i % C::kStages;
       if (i >= C::kStages && !mbar_wait(&empty[s], (uint32_t)((i / C::kStages) - 1) & 1u, kDevTimeoutEmpty)) break;
@@ -160,7 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
       tma_load_2d(st, &wmap, kx, m0, &full[s]);
       tma_load_2d(st + C::kA, &xhi_map, kx, n0, &full[s]);
       tma_load_2d(st + C::kA + C::kB, &xlo_map, kx, n0, &full[s]);
+      issued = i + 1;
     }
+    // After an error the MMA warp may stop consuming: every copy still in flight must
+    // land before the CTA's shared memory is released (each stage's last use is exact).
+    if (issued < nk || error_set())
+      for (int i = issued > C::kStages ? issued - C::kStages : 0; i < issued; ++i)
+        if (!mbar_wait_drain(&full[i % C::kStages], (uint32_t)(i / C::kStages) & 1u)) break;
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer
     for (int i = 0; i < nk; ++i) {

@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const __grid_constant__ Pa
       // Drain: every issued copy must land before the CTA's shared memory is released.
       const int first = it > kStages ? it - kStages : 0;
       for (int i = first; i < it; ++i)
-        if (!mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u, kDevTimeoutDrain)) break;
+        if (!mbar_wait_drain(&full[i % kStages], (uint32_t)(i / kStages) & 1u)) break;
     }
     griddep_wait();
     return;

@@ -97,12 +97,17 @@ struct StepParams {
   unsigned* bar;          // grid barrier counter, zero at launch
   unsigned long long* trace;  // nullable: [G][kTraceFrames * phases][3] globaltimer stamps
   int prefetch_ahead;     // weight tiles prefetched into L2 ahead of the ring (0..kMaxPrefetchAhead)
-  int prestage_kv;        // stage the first K/V page pair of each attention item during QKV
-  int prefetch_kv;        // prefetch the K/V pages of this CTA's attention items into L2 during QKV
   int n_frames;
   int mode0, token0;      // embedding of the first step
   int mode_next;          // embedding of later steps
   int inc_frame, record;  // advance the frame counter / record normed states per step
+  // Per-layer record (debugBackboneLayerByLayer, src/engine.ts:2106-2287) of step dbg_frame
+  // of this launch: dbg [(4L+3)][D] = embed, per layer {attn_norm, attn_out, ffn_norm,
+  // ffn_out}, final_norm, hidden.  Null: no record.
+  float* dbg;
+  int dbg_frame;
+  // Polls before a bounded wait of this kernel gives up (0: the built-in limits).
+  uint32_t wait_limit;
   // tensor parallelism (N > 1)
   int rank;
   float* h2;                          // second residual buffer (h alternates per all-reduce)
@@ -177,11 +182,13 @@ __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long
   return v;
 }
 // Value of a tagged word once its tag is `tag` (bounded poll, as below).
-__device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32_t tag) {
+// Default poll limits of the kernel's waits (StepParams::wait_limit overrides both).
+constexpr uint32_t kTagPolls = 1u << 24, kBarPolls = 1u << 27;
+__device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32_t tag, uint32_t limit) {
   unsigned long long w = ld_tagged(p);
   for (uint32_t i = 0; (uint32_t)(w >> 32) != tag; ++i) {
-    if (i > (1u << 24) || ((i & 1023u) == 1023u && error_set())) {
-      if (i > (1u << 24)) set_error(kDevTimeoutRed);
+    if (i > limit || ((i & 1023u) == 1023u && error_set())) {
+      if (i > limit) set_error(kDevTimeoutPeer);
       break;
     }
     w = ld_tagged(p);
@@ -190,13 +197,13 @@ __device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32
 }
 // Four consecutive tagged words (two 16-byte loads), once all carry `tag` (bounded
 // poll: an expired wait records an error and returns the words' current values).
-__device__ __forceinline__ float4 wait_tagged4(const unsigned long long* p, uint32_t tag) {
+__device__ __forceinline__ float4 wait_tagged4(const unsigned long long* p, uint32_t tag, uint32_t limit) {
   ulonglong2 a = ld_tagged2(p), b = ld_tagged2(p + 2);
   for (uint32_t i = 0; (uint32_t)(a.x >> 32) != tag || (uint32_t)(a.y >> 32) != tag || (uint32_t)(b.x >> 32) != tag ||
                        (uint32_t)(b.y >> 32) != tag;
        ++i) {
-    if (i > (1u << 24) || ((i & 1023u) == 1023u && error_set())) {
-      if (i > (1u << 24)) set_error(kDevTimeoutRed);
+    if (i > limit || ((i & 1023u) == 1023u && error_set())) {
+      if (i > limit) set_error(kDevTimeoutPeer);
       break;
     }
     a = ld_tagged2(p);
@@ -214,10 +221,11 @@ __device__ __forceinline__ float4 wait_tagged4(const unsigned long long* p, uint
 template <int N>
 __device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid, bool skip_grid = false) {
   if (ctid == 0 && !(N > 1 && skip_grid)) {
+    const uint32_t limit = p.wait_limit ? p.wait_limit : kBarPolls;
     uint32_t i = 0;
     while (ld_relaxed(p.bar) < target) {
-      if (++i > (1u << 27) || ((i & 1023u) == 0 && error_set())) {
-        if (i > (1u << 27)) set_error(kDevTimeoutRed);
+      if (++i > limit || ((i & 1023u) == 0 && error_set())) {
+        if (i > limit) set_error(kDevTimeoutBarrier);
         break;
       }
     }
@@ -318,6 +326,7 @@ struct ArIn {
   uint32_t tag;
   unsigned long long* hx;           // [D] tagged words of the summed row (this parity)
   int e0, e1;
+  uint32_t limit;                   // polls before a wait for a peer's words gives up
 };
 __device__ __forceinline__ bool tags_are(const ulonglong2& a, const ulonglong2& b, uint32_t tag) {
   return (uint32_t)(a.x >> 32) == tag && (uint32_t)(a.y >> 32) == tag && (uint32_t)(b.x >> 32) == tag &&
@@ -344,7 +353,7 @@ __device__ __forceinline__ float4 ar_sum4(const ArIn& a, int col) {
       const float4 x = tags_are(w[g][0], w[g][1], a.tag)
                            ? make_float4(__uint_as_float((uint32_t)w[g][0].x), __uint_as_float((uint32_t)w[g][0].y),
                                          __uint_as_float((uint32_t)w[g][1].x), __uint_as_float((uint32_t)w[g][1].y))
-                           : wait_tagged4(a.recv + (long long)(r0 + g) * D + col, a.tag);
+                           : wait_tagged4(a.recv + (long long)(r0 + g) * D + col, a.tag, a.limit);
       v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
     }
   }
@@ -364,7 +373,7 @@ __device__ __forceinline__ void ar_stage_a(const ArIn& a, int t) {
     for (int r = 0; r < N; ++r) w[r] = ld_tagged(a.recv + (long long)r * D + i);
 #pragma unroll
     for (int r = 0; r < N; ++r)
-      v += (uint32_t)(w[r] >> 32) == a.tag ? __uint_as_float((uint32_t)w[r]) : wait_tagged(a.recv + (long long)r * D + i, a.tag);
+      v += (uint32_t)(w[r] >> 32) == a.tag ? __uint_as_float((uint32_t)w[r]) : wait_tagged(a.recv + (long long)r * D + i, a.tag, a.limit);
     a.h_new[i] = v;
     st_tagged(a.hx + i, v, a.tag);
   }
@@ -383,14 +392,14 @@ __device__ __forceinline__ void ar_stage_b(const ArIn& a, const int (&col)[CPL],
     v[j] = tags_are(w[j][0], w[j][1], a.tag)
                ? make_float4(__uint_as_float((uint32_t)w[j][0].x), __uint_as_float((uint32_t)w[j][0].y),
                              __uint_as_float((uint32_t)w[j][1].x), __uint_as_float((uint32_t)w[j][1].y))
-               : wait_tagged4(a.hx + col[j], a.tag);
+               : wait_tagged4(a.hx + col[j], a.tag, a.limit);
 }
 // WK consumer warps split the tile's K columns (chunk j of warp (wr, wk) is
 // column block wk + WK*j), the 8/WK row groups split its R rows.
 template <int R, int CPL, bool NORM, int TG, int WK = kCW, int N = 1>
 __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& it, uint32_t& rit, const float* x,
                                        const __half* norm_w, int kc, int T, int off, int c, int G, int cw, int lane,
-                                       int pos, int f, int kl, const ArIn* ar = nullptr) {
+                                       int pos, int f, int kl, const ArIn* ar = nullptr, int rec_row = -1) {
   constexpr int RW = R / (kCW / WK);   // rows per warp
   static_assert(RW * (kCW / WK) == R && RW * TG <= kMaxVals, "tile rows");
   static_assert(!NORM || WK == kCW, "RMSNorm phases partition the row over all warps");
@@ -448,6 +457,17 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
     for (int j = 0; j < CPL; ++j) {
       xr[j][0] = xr[j][0] * rms * wn[j][0].x; xr[j][1] = xr[j][1] * rms * wn[j][0].y;
       xr[j][2] = xr[j][2] * rms * wn[j][1].x; xr[j][3] = xr[j][3] * rms * wn[j][1].y;
+    }
+  }
+  if (NORM && rec_row >= 0 && p.dbg && f == p.dbg_frame && c == 0) {
+    // per-layer record: the input row (rec_row) and its RMSNorm output (rec_row + 1)
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const int col = (wk + WK * j) * 128 + lane * 4;
+      const float4 raw = N > 1 && ar ? hv[j] : *reinterpret_cast<const float4*>(x + col);
+      *reinterpret_cast<float4*>(p.dbg + (long long)rec_row * D + col) = raw;
+      *reinterpret_cast<float4*>(p.dbg + (long long)(rec_row + 1) * D + col) =
+          make_float4(xr[j][0], xr[j][1], xr[j][2], xr[j][3]);
     }
   }
   trace_mark(p, c, f, kl, 3, p.n_layers, cw * 32 + lane);
@@ -611,31 +631,12 @@ __device__ __forceinline__ void issue_pair(const StepParams& p, const CUtensorMa
     tma_load_2d(dst + 24576, kvmap, 64, vrow, s.afull);
   }
 }
-// Called at the start of the QKV phase: the first page pair of this CTA's attention
-// item holds only positions written by earlier steps (except the current position's
-// row, patched in the attention phase), so its TMA can run under the QKV phase.
-template <int N>
-__device__ __forceinline__ bool prestage(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int pos,
-                                         int c, int ctid, bool& a_pending) {
-  if (!p.prestage_kv || c >= Tp<N>::NKV * p.n_splits) return false;
-  int npages, pps, n_used;
-  split_plan(p, pos, npages, pps, n_used);
-  const int kvh = c / p.n_splits, split = c % p.n_splits;
-  if (split >= n_used) return false;
-  const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
-  if (ctid == 0 && !error_set()) {
-    a_pending = true;
-    issue_pair(p, kvmap, s, layer, kvh, pg0, min(2, pg1 - pg0));
-  }
-  return true;
-}
-
 // Called at the start of the QKV phase: L2 prefetch of the K/V pages of this CTA's
 // attention items, so that the attention phase's TMA loads hit L2.  The current
 // position's row is written later in the QKV phase; L2 stays coherent with that write.
 template <int N>
 __device__ __forceinline__ void prefetch_kv(const StepParams& p, int layer, int pos, int c, int G, int ctid) {
-  if (!p.prefetch_kv || ctid != 0) return;
+  if (ctid != 0) return;
   int npages, pps, n_used;
   split_plan(p, pos, npages, pps, n_used);
   const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
@@ -655,7 +656,7 @@ __device__ __forceinline__ void prefetch_kv(const StepParams& p, int layer, int 
 // reached by all of them); after a device error the work is skipped, not the barriers.
 template <int N>
 __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap* kvmap, Smem& s, uint32_t& ait,
-                                          bool& a_pending, bool staged, int layer, int pos, int c, int G, int cw,
+                                          bool& a_pending, int layer, int pos, int c, int G, int cw,
                                           int lane, int ctid) {
   const int seq = pos + 1;
   int npages, pps, n_used;
@@ -677,8 +678,7 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
     for (int pp = pg0; pp < pg1; pp += 2) {
       const int npair = min(2, pg1 - pp);
       const bool go = !error_set();
-      const bool pre = staged && item == c && pp == pg0;   // already in flight since the QKV phase
-      if (ctid == 0 && go && !pre) {
+      if (ctid == 0 && go) {
         a_pending = true;
         issue_pair(p, kvmap, s, layer, kvh, pp, npair);
       }
@@ -701,22 +701,6 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
       const bool w_ok = go && mbar_wait(s.afull, ait & 1u, kDevTimeoutFull);
       if (w_ok && ctid == 0) a_pending = false;
       ++ait;
-      if (pre) {
-        // the current position's K/V row was written during the QKV phase: patch it
-        const int cp = pos / 64 - pp;
-        if (cp >= 0 && cp < npair) {
-          named_bar_sync(1, kCW * 32);
-          if (ctid < 32 && w_ok) {
-            const int kv = ctid >> 4, ch = ctid & 15, r = pos & 63;
-            const int phys = ptab[pp + cp];
-            const uint4 v = *reinterpret_cast<const uint4*>(
-                p.kv.pool + gemv::kv_row(p.kv, phys, layer, kv, kvh, r) * HD + ch * 8);
-            *reinterpret_cast<uint4*>(s.attn + cp * 32768 + kv * 16384 + (ch >> 3) * 8192 + r * 128 +
-                                      (((ch & 7) ^ (r & 7)) << 4)) = v;
-          }
-          named_bar_sync(1, kCW * 32);
-        }
-      }
       if (w_ok && half_pair < npair) {
         const int pg = pp + half_pair;
         const uint32_t kbase = smem_u32(s.attn + half_pair * 32768);
@@ -938,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       // drain the copies still in flight
       const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0u;
       for (uint32_t i = first; i < it; ++i)
-        if (!mbar_wait(&s.full[i % kStages], (i / kStages) & 1u, kDevTimeoutDrain)) break;
+        if (!mbar_wait_drain(&s.full[i % kStages], (i / kStages) & 1u)) break;
     }
     return;
   }
@@ -998,11 +982,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   float* const hb[2] = {p.h, N > 1 ? p.h2 : p.h};
   auto ar_in = [&](unsigned long long k) {
     return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1], (uint32_t)(k + 1),
-                p.hx + (long long)(k & 1) * D, e0, e1};
+                p.hx + (long long)(k & 1) * D, e0, e1, p.wait_limit ? p.wait_limit : kTagPolls};
   };
   for (int f = 0; f < p.n_frames; ++f) {
     const int pos = pos0 + f, frame = frame0 + f;
     const unsigned long long kf = p.ar_base + 2ull * L * f;
+    const bool rec = p.dbg && f == p.dbg_frame;   // per-layer record of this step
     // ---- EMBED
     grid_wait<N>(p, phase * G, ctid);
     trace_mark(p, c, f, 0, 0, L, ctid);
@@ -1040,6 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
           v = a;
         }
         p.h[i] = v;
+        if (rec) p.dbg[i] = v;
       }
       named_bar_sync(1, kCW * 32);
       if (ctid == 0) red_release_add(p.bar, 1u);
@@ -1057,19 +1043,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       const bool ar_qkv = N > 1 && l > 0;
       grid_wait<N>(p, phase * G, ctid, ar_qkv);
       trace_mark(p, c, f, kl, 0, L, ctid);
-      const bool staged = prestage<N>(p, &kvmap, s, l, pos, c, ctid, a_pending);
       prefetch_kv<N>(p, l, pos, c, G, ctid);
       {
         const ArIn a = ar_qkv ? ar_in(k_prev) : ArIn{};
         consume<6, 3, true, kTgQKV, kCW, N>(p, s, it, rit, hb[0], W.attn_norm, D, TD::TQKV, o0, c, G, cw, lane, pos, f,
-                                            kl, ar_qkv ? &a : nullptr);
+                                            kl, ar_qkv ? &a : nullptr, 4 * l);
       }
       trace_mark(p, c, f, kl, 1, L, ctid);
       ++phase;
       // ---- attention
       grid_wait<N>(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 1, 0, L, ctid);
-      attention<N>(p, &kvmap, s, ait, a_pending, staged, l, pos, c, G, cw, lane, ctid);
+      attention<N>(p, &kvmap, s, ait, a_pending, l, pos, c, G, cw, lane, ctid);
       trace_mark(p, c, f, kl + 1, 1, L, ctid);
       if (ctid == 0) red_release_add(p.bar, 1u);
       ++phase;
@@ -1086,7 +1071,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       {
         const ArIn a = N > 1 ? ar_in(k_o) : ArIn{};
         consume<6, 3, true, kTgW13, kCW, N>(p, s, it, rit, hb[0], W.ffn_norm, D, TD::TW13, o2, c, G, cw, lane, pos, f,
-                                            kl + 3, N > 1 ? &a : nullptr);
+                                            kl + 3, N > 1 ? &a : nullptr, 4 * l + 2);
       }
       trace_mark(p, c, f, kl + 3, 1, L, ctid);
       ++phase;
@@ -1145,9 +1130,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       float* ring = (p.record && frame >= 0 && frame < st.max_frames)
                         ? p.normed_ring + ((long long)p.slot * st.max_frames + frame) * D : nullptr;
       for (int i = e0 + ctid; i < e1; i += kCW * 32) {
-        const float v = hval(i) * rms * __half2float(p.final_norm[i]);
+        const float hi = hval(i);
+        const float v = hi * rms * __half2float(p.final_norm[i]);
         p.normed[i] = v;
         if (ring) ring[i] = v;
+        if (rec) {   // last layer's ffn_out, final_norm, hidden
+          p.dbg[(long long)(4 * L) * D + i] = hi;
+          p.dbg[(long long)(4 * L + 1) * D + i] = v;
+          p.dbg[(long long)(4 * L + 2) * D + i] = hi;
+        }
       }
       named_bar_sync(1, kCW * 32);
       if (ctid == 0) red_release_add(p.bar, 1u);
@@ -1155,7 +1146,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     }
   }
   // an attention copy left in flight by an error must land before the CTA exits
-  if (ctid == 0 && a_pending) mbar_wait(s.afull, (ait - 1) & 1u, kDevTimeoutDrain);
+  if (ctid == 0 && a_pending) mbar_wait_drain(s.afull, (ait - 1) & 1u);
   // slot bookkeeping once every CTA has finished the last step
   if (c == 0) {
     grid_wait<N>(p, phase * G, ctid);

@@ -24,6 +24,8 @@ enum DevError : int {
   kDevTimeoutDrain = 4,   // waiting for in-flight copies at exit expired
   kDevBadIndex = 5,       // an index from device memory was out of range
   kDevTimeoutAcc = 6,     // tensor-core accumulator (tcgen05.commit) wait expired
+  kDevTimeoutPeer = 7,    // a tensor-parallel peer's all-reduce words did not arrive
+  kDevTimeoutBarrier = 8, // a grid barrier of the persistent kernel was not reached by every CTA
 };
 
 __device__ int vx_dev_error;
@@ -73,6 +75,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
     if ((i & 1023u) == 1023u && error_set()) return false;
   }
   set_error(code);
+  return false;
+}
+
+// Wait for copies already in flight before a CTA exits.  A bulk copy from valid memory
+// always completes, so this wait does not give up when another wait has recorded an
+// error (mbar_wait does): the CTA must not exit while a copy still targets its shared
+// memory.  Still bounded.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  set_error(kDevTimeoutDrain);
   return false;
 }
 

@@ -86,7 +86,6 @@ struct vx_handle {
   vx_config cfg{};
   int dev = 0, num_sms = 148;
   cudaStream_t own_stream = nullptr, stream = nullptr;
-  bool use_pdl = true;
   std::string err;
   long long launches = 0;
 
@@ -165,19 +164,19 @@ struct vx_handle {
   mk::LayerPtrs* d_layers = nullptr;
   unsigned* d_bar = nullptr;
   unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
-  int prefetch_ahead = 3;   // persistent kernel: L2 lookahead in weight tiles (VX_PREFETCH_AHEAD; measured best)
-  int prestage_kv = 0;      // persistent kernel: stage K/V pages during QKV (VX_PRESTAGE_KV=1; measured slower)
-  int prefetch_kv = 1;      // persistent kernel: L2 prefetch of the attention items' K/V pages during QKV (VX_PREFETCH_KV; measured -0.3 %)
+  int prefetch_ahead = 3;   // persistent kernel: L2 lookahead in weight tiles (option l2_prefetch_tiles; measured best)
+  uint32_t wait_limit = 0;  // persistent kernel: polls before a barrier / peer wait gives up (option wait_limit; 0 = built-in)
+  bool tp_loopback = false; // option tp_loopback: every peer receive buffer is this handle's own (test support)
   bool trace_armed = false;
 
   // token batches on the tensor cores (k_gemm.cuh): batched prefill
-  bool use_tb = true;                  // VX_NO_BATCHED_PREFILL=1: no token-batch path (token-by-token prefill)
-  bool prefill_tokenwise = false;      // VX_PREFILL_TOKENWISE=1: token-by-token prefill, batch path kept
+  bool use_tb = true;                  // token-batch path (tensor-core GEMMs; tp 1)
+  bool prefill_tokenwise = false;      // option batched_prefill = 0: token-by-token prefill
   int tb_cap = 0;                      // rows per batch
   struct TbLayerMaps { CUtensorMap wqkv, wo, w13, w2; };
   std::vector<TbLayerMaps> tb_wmaps;   // per backbone layer
   std::vector<TbLayerMaps> fm_wmaps;   // per acoustic-transformer layer (fm_tc)
-  bool fm_tc = false;                  // acoustic transformer on the tensor-core GEMM (VX_FM_GEMV=1: per-op GEMVs)
+  bool fm_tc = false;                  // acoustic transformer on the tensor-core GEMM (tp 1; per-op GEMVs otherwise)
   CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl (128-row boxes)
   CUtensorMap tb_xhi64[3], tb_xlo64[3];  // the same with 64-row boxes (batches of <= 64 rows)
   CUtensorMap tb_xhi16[3], tb_xlo16[3];  // and 16-row boxes (the acoustic transformer's 6 rows)
@@ -187,7 +186,6 @@ struct vx_handle {
   int* tb_att_tickets = nullptr;
   __half *tb_hi = nullptr, *tb_lo = nullptr;
   size_t tb_ws_floats = 0;
-  int tb_attn_splits = 0;              // attention splits per (slot, KV head) in batched decode; 0: by context length
 
   // vx_profile_step: which kernels a captured step contains, and the GEMV bytes it moves
   int parts = 7;          // kPartMisc | kPartGemv | kPartAttn
@@ -224,7 +222,7 @@ cudaError_t launch(vx_handle* h, void (*kern)(KArgs...), dim3 grid, dim3 block, 
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = h->use_pdl ? 1 : 0;
+  cfg.numAttrs = 1;
   h->launches++;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
@@ -275,7 +273,7 @@ constexpr size_t kP2pHxOff = 2ull * mk::kMaxTp * 3072 * 8;
 constexpr size_t kP2pBytes = kP2pHxOff + 2ull * 3072 * 8;
 
 int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, int mode_next, bool inc_frame,
-                 bool record) {
+                 bool record, float* dbg = nullptr, int dbg_frame = -1) {
   if (n_frames <= 0) return VX_OK;
   mk::StepParams sp{};
   sp.layers = h->d_layers; sp.n_layers = h->L;
@@ -293,8 +291,8 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
   sp.slots = h->slots; sp.slot = slot; sp.bar = h->d_bar;
   sp.trace = h->trace_armed ? h->d_trace : nullptr;
   sp.prefetch_ahead = h->prefetch_ahead;
-  sp.prestage_kv = h->prestage_kv;
-  sp.prefetch_kv = h->prefetch_kv;
+  sp.dbg = dbg; sp.dbg_frame = dbg_frame;
+  sp.wait_limit = h->wait_limit;
   h->trace_armed = false;
   sp.n_frames = n_frames; sp.mode0 = mode0; sp.token0 = token0; sp.mode_next = mode_next;
   sp.inc_frame = inc_frame ? 1 : 0; sp.record = record ? 1 : 0;
@@ -407,8 +405,10 @@ int check_device_error(vx_handle* h) {
     cudaMemcpyToSymbol(vx::vx_dev_error, &z, sizeof(int));
     static const char* names[] = {"ok", "TMA stage wait expired", "free-stage wait expired",
                                   "reduction slot wait expired", "drain wait expired", "index out of range",
-                                  "tensor-core accumulator wait expired"};
-    return h->fail(VX_E_DEVICE, "device-side error: %s", (e > 0 && e < 7) ? names[e] : "unknown");
+                                  "tensor-core accumulator wait expired",
+                                  "tensor-parallel peer wait expired (a peer's all-reduce words did not arrive)",
+                                  "grid barrier wait expired"};
+    return h->fail(VX_E_DEVICE, "device-side error: %s", (e > 0 && e < 9) ? names[e] : "unknown");
   }
   return VX_OK;
 }
@@ -856,14 +856,11 @@ int enqueue_decode_batch_bn(vx_handle* h, int slot0, int n, int nsb) {
 // waves of 3 CTAs per SM once the context is long, at least 8 pages per split (at
 // short context one split per item, which writes its output without a merge).  The
 // partials hold tb_cap x n_kv x 1 split, so n rows x nsb splits must fit.
-// VX_BATCH_ATTN_SPLITS overrides.
 int batch_attn_splits(vx_handle* h, int slot0, int n) {
   int max_pos = 0;
   for (int s = slot0; s < slot0 + n; ++s) max_pos = std::max(max_pos, h->pos_host[s]);
   const int pages = max_pos / kPage + 1;
-  const int want = h->tb_attn_splits > 0
-                       ? h->tb_attn_splits
-                       : std::max(1, std::min((6 * h->num_sms + h->NKV * n - 1) / (h->NKV * n), pages / 8));
+  const int want = std::max(1, std::min((6 * h->num_sms + h->NKV * n - 1) / (h->NKV * n), pages / 8));
   return std::max(1, std::min({want, h->tb_cap / n, attn::kMaxSplits}));
 }
 
@@ -1012,7 +1009,6 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     rc = bad("bad acoustic-transformer config");
   if (rc) { *out = h; return rc; }
 
-  if (const char* e = getenv("VX_NO_PDL")) h->use_pdl = !(e[0] == '1');
   h->dev = c.device;
   if (cudaSetDevice(h->dev) != cudaSuccess) { *out = h; return h->fail(VX_E_CUDA, "cudaSetDevice(%d) failed", h->dev); }
   cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->dev);
@@ -1220,22 +1216,13 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     h->d_bar = reinterpret_cast<unsigned*>((reinterpret_cast<uintptr_t>(h->d_bar) + 127) & ~uintptr_t(127));
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->dev);
-    if (const char* pa = getenv("VX_PREFETCH_AHEAD")) h->prefetch_ahead = std::max(0, std::min(mk::kMaxPrefetchAhead, atoi(pa)));
-    if (const char* ps = getenv("VX_PRESTAGE_KV")) h->prestage_kv = atoi(ps) != 0;
-    if (const char* pk = getenv("VX_PREFETCH_KV")) h->prefetch_kv = atoi(pk) != 0;
-    const char* e = getenv("VX_NO_MEGAKERNEL");
-    h->coop = coop != 0 && !(e && e[0] == '1');
+    h->coop = coop != 0;
     h->use_mk = h->coop && h->tp == 1;   // TP: enabled by vx_tp_p2p_open
   }
   {
-    const char* e = getenv("VX_NO_BATCHED_PREFILL");
-    h->use_tb = h->tp == 1 && !(e && e[0] == '1');
-    if (const char* as = getenv("VX_BATCH_ATTN_SPLITS")) h->tb_attn_splits = std::max(1, std::min(64, atoi(as)));
-    const char* tw = getenv("VX_PREFILL_TOKENWISE");
-    h->prefill_tokenwise = tw && tw[0] == '1';
+    h->use_tb = h->tp == 1;
     if (h->use_tb && (rc = setup_tb(h))) { *out = h; return rc; }
-    const char* fg = getenv("VX_FM_GEMV");
-    h->fm_tc = h->use_tb && c.enable_fm && !(fg && fg[0] == '1');
+    h->fm_tc = h->use_tb && c.enable_fm;
   }
   *out = h;
   return VX_OK;
@@ -1683,9 +1670,14 @@ int vx_debug_layers(vx_handle* h, int32_t slot, int32_t token, float* out) {
   if (token < 0 || token >= h->V) return h->fail(VX_E_RANGE, "token out of range");
   if ((rc = need_positions(h, slot, 1))) return rc;
   CK(cudaSetDevice(h->dev));
-  if ((rc = set_slot_fields(h, slot, kEmbToken, token))) return rc;
-  DebugSink sink{h->dbg};
-  if ((rc = enqueue_backbone(h, slot, false, false, &sink))) return rc;
+  if (h->use_mk) {
+    // the persistent decode kernel that vx_decode / vx_prefill run, recording this step
+    if ((rc = launch_steps(h, slot, 1, kEmbToken, token, kEmbToken, false, false, h->dbg, 0))) return rc;
+  } else {
+    if ((rc = set_slot_fields(h, slot, kEmbToken, token))) return rc;
+    DebugSink sink{h->dbg};
+    if ((rc = enqueue_backbone(h, slot, false, false, &sink))) return rc;
+  }
   h->pos_host[slot] += 1;
   const size_t n = (size_t)(4 * h->L + 3) * h->D;
   CK(cudaMemcpyAsync(out, h->dbg, n * 4, cudaMemcpyDeviceToHost, h->stream));
@@ -1741,6 +1733,26 @@ int vx_decode(vx_handle* h, int32_t slot, int32_t n_frames, int32_t with_fm) {
   }
   h->frame_host[slot] = f0 + n_frames;
   return VX_OK;
+}
+
+int vx_decode_record(vx_handle* h, int32_t slot, int32_t n_frames, int32_t record_frame, float* out) {
+  int rc = check_slot(h, slot);
+  if (rc) return rc;
+  if (!out || n_frames < 1 || record_frame < 0 || record_frame >= n_frames)
+    return h->fail(VX_E_INVALID, "record_frame %d outside [0, n_frames %d)", record_frame, n_frames);
+  if (!h->use_mk) return h->fail(VX_E_STATE, "vx_decode_record needs the persistent decode kernel");
+  const int f0 = h->frame_host[slot];
+  if (f0 + n_frames > h->cfg.max_frames)
+    return h->fail(VX_E_RANGE, "frames %d + %d exceed the code ring (%d)", f0, n_frames, h->cfg.max_frames);
+  if ((rc = need_positions(h, slot, n_frames))) return rc;
+  CK(cudaSetDevice(h->dev));
+  if (f0 == 0) rc = launch_steps(h, slot, n_frames, kEmbToken, kAudioKick, kEmbSynthCodes, true, true, h->dbg, record_frame);
+  else rc = launch_steps(h, slot, n_frames, kEmbSynthCodes, 0, kEmbSynthCodes, true, true, h->dbg, record_frame);
+  if (rc) return rc;
+  h->pos_host[slot] += n_frames;
+  h->frame_host[slot] = f0 + n_frames;
+  CK(cudaMemcpyAsync(out, h->dbg, (size_t)(4 * h->L + 3) * h->D * 4, cudaMemcpyDeviceToHost, h->stream));
+  return finish(h);
 }
 
 int vx_fill_kv(vx_handle* h, int32_t slot, int32_t n_positions, uint64_t seed) {
@@ -1924,6 +1936,46 @@ int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n, int32_t* dims)
   if (!out || !h->d_trace) return h->fail(VX_E_STATE, "no trace recorded");
   CK(cudaMemcpyAsync(out, h->d_trace, std::min(n, total) * 8, cudaMemcpyDeviceToHost, h->stream));
   return finish(h);
+}
+
+int vx_set_option(vx_handle* h, const char* name, int64_t value) {
+  if (!h || !name) return VX_E_INVALID;
+  const std::string n = name;
+  if (n == "persistent_decode") {
+    if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "persistent_decode must be 0 or 1");
+    if (value && !h->coop) return h->fail(VX_E_STATE, "the device has no cooperative launch");
+    if (value && h->tp > 1 && !h->p2p_ready) return h->fail(VX_E_STATE, "tensor parallelism: call vx_tp_p2p_open first");
+    h->use_mk = value != 0;
+  } else if (n == "batched_prefill") {
+    if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "batched_prefill must be 0 or 1");
+    if (value && !h->use_tb) return h->fail(VX_E_STATE, "batched prefill needs tp_size 1");
+    h->prefill_tokenwise = value == 0;
+  } else if (n == "l2_prefetch_tiles") {
+    if (value < 0 || value > mk::kMaxPrefetchAhead)
+      return h->fail(VX_E_RANGE, "l2_prefetch_tiles must lie in [0, %d]", mk::kMaxPrefetchAhead);
+    h->prefetch_ahead = (int)value;
+  } else if (n == "wait_limit") {
+    if (value < 0 || value > 0xffffffffll) return h->fail(VX_E_RANGE, "wait_limit must lie in [0, 2^32)");
+    h->wait_limit = (uint32_t)value;
+  } else if (n == "tp_loopback") {
+    if (value != 1) return h->fail(VX_E_INVALID, "tp_loopback can only be switched on");
+    if (h->tp < 2) return h->fail(VX_E_STATE, "tp_loopback needs tp_size > 1");
+    if (h->p2p_ready) return h->fail(VX_E_STATE, "peer buffers are already open");
+    if (!h->coop) return h->fail(VX_E_STATE, "the device has no cooperative launch");
+    CK(cudaSetDevice(h->dev));
+    if (!h->p2p_buf) {
+      CK(cudaMalloc(&h->p2p_buf, kP2pBytes));
+      CK(cudaMemset(h->p2p_buf, 0, kP2pBytes));
+      CK(cudaDeviceSynchronize());
+    }
+    for (int r = 0; r < h->tp; ++r) h->p2p_peer[r] = h->p2p_buf;
+    h->tp_loopback = true;
+    h->p2p_ready = true;
+    h->use_mk = true;
+  } else {
+    return h->fail(VX_E_INVALID, "unknown option '%s'", name);
+  }
+  return VX_OK;
 }
 
 int vx_nccl_unique_id(const char* lib, uint8_t out[128]) {

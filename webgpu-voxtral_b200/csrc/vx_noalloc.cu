@@ -104,8 +104,10 @@ __global__ void __launch_bounds__(256) k_lm_head_argmax_noalloc(const __half* __
   if (threadIdx.x == 0) {
     Best f = wbest[0];
     for (int w = 1; w < 8; ++w) f = better(f, wbest[w]);
-    *out_idx = f.i;
-    if (out_val) *out_val = f.v;
+    // NaN products never win; if every product is NaN no row was chosen: report -1
+    const bool none = f.i == 0x7fffffff;
+    *out_idx = none ? -1 : f.i;
+    if (out_val) *out_val = none ? __int_as_float(0x7fc00000) : f.v;
   }
 }
 

@@ -54,6 +54,11 @@ def max_over_ranks(x: float) -> float:
     return float(t.item())
 
 
+def min_over_ranks(x: float) -> float:
+    """Minimum of a host float over all ranks (a rate: the job runs at its slowest rank)."""
+    return -max_over_ranks(-float(x))
+
+
 def sum_over_ranks(x: float) -> float:
     if not (dist.is_available() and dist.is_initialized()):
         return float(x)

@@ -120,6 +120,8 @@ def load_library():
         "vx_tp_init": (ctypes.c_int, [H, ctypes.c_char_p, _u8p]),
         "vx_tp_p2p_handle": (ctypes.c_int, [H, _u8p]),
         "vx_tp_p2p_open": (ctypes.c_int, [H, _u8p]),
+        "vx_set_option": (ctypes.c_int, [H, ctypes.c_char_p, ctypes.c_int64]),
+        "vx_decode_record": (ctypes.c_int, [H, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f32p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -321,6 +323,11 @@ class VoxtralEngine:
     def synchronize(self):
         self._check(load_library().vx_synchronize(self._h))
 
+    def set_option(self, name: str, value: int):
+        """Engine option of vx_set_option (persistent_decode, batched_prefill, l2_prefetch_tiles,
+        wait_limit, tp_loopback)."""
+        self._check(load_library().vx_set_option(self.handle, name.encode(), int(value)))
+
     def launch_count(self) -> int:
         return int(load_library().vx_launch_count(self._h))
 
@@ -467,6 +474,14 @@ class VoxtralEngine:
         """Enqueue n_frames device-resident frames (no host round trip); asynchronous."""
         self._require_ready()
         self._check(load_library().vx_decode(self._h, slot, n_frames, int(with_fm)))
+
+    def decode_record(self, n_frames: int, record_frame: int, slot: int = 0) -> np.ndarray:
+        """Backbone-only decode of n_frames frames (as decode(n, with_fm=False)) that returns the
+        per-layer tensors of frame record_frame, rows as in debugBackboneLayerByLayer's "raw"."""
+        self._require_ready()
+        out = np.empty((4 * self._cfg.n_layers + 3, self._cfg.dim), np.float32)
+        self._check(load_library().vx_decode_record(self._h, slot, n_frames, record_frame, _p(out, _f32p)))
+        return out
 
     def decode_batch(self, n_frames: int, n_slots: int, slot0: int = 0):
         """Backbone-only decode of n_frames frames for slots [slot0, slot0+n_slots) in lockstep
