@@ -263,16 +263,23 @@ def run_c4(args, vx, synth, local, stream, vdist, rank, world):
                        "note": "2 flops per weight per slot; the tensor cores run twice that (activations as f16 hi + lo)"}}
 
 
-def run_c5(args, vx, local, stream):
-    """C5 on one GPU: S utterances whose K/V cache holds P synthetic
-    positions (f16 N(0,1), vx_fill_kv), decoded F frames in lockstep (vx_decode_batch,
-    split-KV attention).  The KV stream dominates: S * P * 106,496 bytes per step."""
+def run_c5(args, vx, local, stream, vdist, rank, tp):
+    """C5: S utterances whose K/V cache holds P synthetic positions (f16
+    N(0,1), vx_fill_kv), decoded F frames in lockstep (vx_decode_batch, split-KV
+    attention).  The KV stream dominates: S * P * 106,496 bytes per step.  With tp > 1
+    the utterances are decoded tensor-parallel over the ranks: each GPU holds 8/tp KV
+    heads of every utterance (1 at TP-8) and 1/tp of the weights, with an NCCL
+    all-reduce after o_proj and after down in every layer."""
     import torch
     S, P, F5 = args.c5_slots, args.c5_context, args.c5_frames
     eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": args.layers}}, "maxSeqLen": P + F5 + 8,
-                            "maxFrames": F5 + 8, "enableFM": False, "device": local, "maxSlots": S,
-                            "maxVoiceRows": 1})
+                            "maxFrames": F5 + 8, "enableFM": False, "enableCodec": False, "device": local,
+                            "maxSlots": S, "maxVoiceRows": 1, "tpSize": tp, "tpRank": rank if tp > 1 else 0})
     eng.init()
+    if tp > 1:
+        lib = nccl_lib_path()
+        uid = vdist.broadcast_bytes(vx.nccl_unique_id(lib) if rank == 0 else None)
+        vx.tp_init(eng, uid, lib, p2p=False)
     eng.loadRandomWeights(0)
     eng.set_stream(stream.cuda_stream)
     for u in range(S):
@@ -284,22 +291,26 @@ def run_c5(args, vx, local, stream):
     for u in range(S):
         eng.rewind(slot=u)
     torch.cuda.synchronize()
+    vdist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     eng.decode_batch(F5, S)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    vdist.barrier()
+    ms = vdist.max_over_ranks(e0.elapsed_time(e1))
     eng.destroy()
     step_ms = ms / F5
     avg_pos = P + (F5 - 1) / 2
-    kv = S * (avg_pos + 1) * KV_BYTES_PER_POS * args.layers / 26
-    step_bytes = args.layers * BYTES_PER_LAYER + 6144 + S * 37 * 3072 * 2 + kv
+    kv = S * (avg_pos + 1) * KV_BYTES_PER_POS * args.layers / 26 / tp
+    step_bytes = (args.layers * BYTES_PER_LAYER + 6144) / tp + S * 37 * 3072 * 2 + kv
     peak, kind = measured_peaks()
-    return {"workload": f"C5 on one GPU: {S} utterances with {P} synthetic f16 K/V positions each (vx_fill_kv), "
+    where = "one GPU" if tp == 1 else f"TP-{tp} (1/{tp} of the KV heads and weights per GPU, NCCL all-reduce x2 per layer)"
+    return {"workload": f"C5 on {where}: {S} utterances with {P} synthetic f16 K/V positions each (vx_fill_kv), "
                         f"{F5} frames in lockstep, split-KV flash-decode over the paged cache",
             "frames_per_s": S * F5 / (ms / 1e3), "ms_per_step": step_ms, "slots": S, "frames": F5,
-            "avg_position": avg_pos, "kv_bytes_per_step": kv,
+            "parallelism": f"tp{tp}" if tp > 1 else "single GPU",
+            "avg_position": avg_pos, "kv_bytes_per_step_per_gpu": kv,
             "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": step_bytes,
                          "achieved": step_bytes / (step_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": step_bytes / (step_ms / 1e3) / 1e9 / peak, "peak_kind": kind}}
@@ -493,8 +504,8 @@ def run_b200(args):
         codec = run_codec(args, vx, local, stream)
 
     c5 = None
-    if args.c5_frames > 0 and tp == 1:
-        c5 = run_c5(args, vx, local, stream)
+    if args.c5_frames > 0:
+        c5 = run_c5(args, vx, local, stream, vdist, rank, tp)
 
     # ------------------------------------------------------------------ end to end through the C ABI
     e2e_vals, h2d, d2h = [], 0, 0

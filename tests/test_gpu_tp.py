@@ -19,6 +19,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 TOL = 2e-2
 DEC_FRAMES = 8
+C5_POS, C5_FRAMES = 3000, 4
 
 
 def _free_port() -> int:
@@ -59,6 +60,11 @@ def _rank_main(rank, world, port, q):
         vx.tp_init(eng, uid, lib)
         eng.loadRandomWeights(0)
         eng.prefill(g["tokens"], int(g["audio_start"]), int(g["audio_count"]), g["voice"])
+        pos0 = eng.position()
+        am = eng.backboneStepAndRead(24)   # vocab-sharded LM head + argmax all-reduce
+        eng.reset()
+        eng.prefill(g["tokens"], int(g["audio_start"]), int(g["audio_count"]), g["voice"])
+        assert eng.position() == pos0
         kick = eng.debugBackboneLayerByLayer(24)["raw"]
         f0 = eng.debugFMStep(g["noise"][0])
         worst = max(float(np.max(np.abs(kick[i] - g["kick_debug"][i])) / np.max(np.abs(g["kick_debug"][i])))
@@ -72,8 +78,24 @@ def _rank_main(rank, world, port, q):
         eng.prefill(toks, a0, na, synth.voice_rows(2, 20))
         eng.decode(DEC_FRAMES, with_fm=False)
         normed = eng.read_normed(0, DEC_FRAMES)
-        q.put((rank, "ok", worst, lrel, f0["semantic_code"], int(g["f0_semantic_code"]), normed))
         eng.destroy()
+        # long-context form (C5) under TP: batched decode over a synthetic context, the
+        # KV heads sharded over the ranks, NCCL all-reduces after o_proj and down
+        e2 = vx.VoxtralEngine({"config": {"backbone": {"n_layers": 2}}, "maxSeqLen": C5_POS + 16, "maxFrames": 16,
+                               "enableFM": False, "enableCodec": False, "maxSlots": 2, "maxVoiceRows": 1,
+                               "device": rank, "tpSize": world, "tpRank": rank})
+        e2.init()
+        uid2 = vdist.broadcast_bytes(vx.nccl_unique_id(lib) if rank == 0 else None)
+        vx.tp_init(e2, uid2, lib, p2p=False)
+        e2.loadRandomWeights(0)
+        for s in range(2):
+            e2.reset(slot=s)
+            e2.set_streams(noise_seed=3, codes_seed=4, utt=40 + s, slot=s)
+            e2.fill_kv(C5_POS, seed=100 + s, slot=s)
+        e2.decode_batch(C5_FRAMES, 2)
+        c5 = e2.read_normed(0, C5_FRAMES, slot=1)
+        e2.destroy()
+        q.put((rank, "ok", worst, lrel, f0["semantic_code"], int(g["f0_semantic_code"]), normed, c5, am))
         vdist.barrier()
         vdist.shutdown()
     except Exception as e:  # noqa: BLE001
@@ -106,13 +128,24 @@ def test_tp_matches_golden(world):
     ref = o.generate(toks, a0, na, synth.voice_rows(2, 20), DEC_FRAMES,
                      codes_in=synth.feedback_codes(6, 0, DEC_FRAMES), want_normed=True)
     o.close()
+    o = oracle.Oracle(n_layers=2, max_seq=C5_POS + 16, with_fm=False)
+    o.fill_kv(C5_POS, seed=101)
+    codes = synth.feedback_codes(41, 0, C5_FRAMES)
+    ref5 = [o.backbone_step(24)["normed"]]
+    for f in range(1, C5_FRAMES):
+        ref5.append(o.backbone_step(embed=o.multi_codebook_embed(int(codes[f - 1][0]), codes[f - 1][1:]))["normed"])
+    o.close()
+    g = np.load(os.path.join(ROOT, "tests", "golden", "c1_small.npz"))
     for r in out:
-        _, _, worst, lrel, sem, want, normed = r
+        _, _, worst, lrel, sem, want, normed, c5, am = r
+        assert am == int(g["kick_argmax"]), (r[0], am)
         assert worst < TOL, worst
         assert lrel < TOL, lrel
         assert sem == want
         for f in range(DEC_FRAMES):
             assert max_abs_rel(normed[f], ref["normed"][f]) < TOL, (r[0], f)
+        for f in range(C5_FRAMES):
+            assert max_abs_rel(c5[f], ref5[f]) < TOL, ("c5", r[0], f)
     # every rank holds the same residual stream: identical outputs
     for r in out[1:]:
         assert np.array_equal(out[0][6], r[6])

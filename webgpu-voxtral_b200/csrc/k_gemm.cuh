@@ -337,6 +337,8 @@ struct RowParams {
   float eps;
   __half *hi, *lo;           // [N][M]
   RopeKvParams rope;         // kRowQkv (rope.qkv unused)
+  const float* add;          // kRowResidNorm with splits == 0: h[n] += add[n] ([N][M], e.g. an all-reduced
+                             // tensor-parallel partial); null: Y already holds h[n]
 };
 // Launched with M / 4, M / 8 or M / 12 threads per row (a multiple of 32, at most
 // 1024): each thread owns 1-3 float4 groups and issues the loads of every split at
@@ -358,6 +360,11 @@ __global__ void __launch_bounds__(1024) k_tb_row(const __grid_constant__ RowPara
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.splits == 0) {
       acc = *reinterpret_cast<const float4*>(p.y + (long long)n * p.ldy + m);
+      if (p.mode == kRowResidNorm && p.add) {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(p.add + (long long)n * p.M + m));
+        acc = make_float4(acc.x + a.x, acc.y + a.y, acc.z + a.z, acc.w + a.w);
+        *reinterpret_cast<float4*>(p.y + (long long)n * p.ldy + m) = acc;
+      }
     } else {
       const int tile = (m / kBM) * p.n_tiles + n / p.bn;
       const float* src = p.ws + ((long long)tile * p.splits * p.bn + n % p.bn) * kBM + m % kBM;

@@ -353,6 +353,21 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* x, int n, int32_t*
   }
 }
 
+// Vocab-sharded LM head under tensor parallelism: this rank's argmax (index `local`
+// into its logits, rows [row0, row0 + n) of the vocabulary) as a 64-bit key whose
+// maximum over the ranks is the global argmax with k_argmax's rule (maximum value,
+// lowest index on ties): high word = the value's bits mapped to an order-preserving
+// unsigned, low word = ~(global index).
+__global__ void k_argmax_key(const float* logits, const int32_t* local, int row0, unsigned long long* key) {
+  griddep_launch();
+  griddep_wait();
+  if (threadIdx.x != 0) return;
+  const int i = *local;
+  const uint32_t b = __float_as_uint(logits[i]);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  *key = ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)(row0 + i));
+}
+
 // ------------------------------------------------------------------ FM
 struct FmParams {
   SlotState* slots;

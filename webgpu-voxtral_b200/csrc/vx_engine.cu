@@ -170,7 +170,7 @@ struct vx_handle {
   bool trace_armed = false;
 
   // token batches on the tensor cores (k_gemm.cuh): batched prefill
-  bool use_tb = true;                  // token-batch path (tensor-core GEMMs; tp 1)
+  bool use_tb = true;                  // token-batch path (tensor-core GEMMs)
   bool prefill_tokenwise = false;      // option batched_prefill = 0: token-by-token prefill
   int tb_cap = 0;                      // rows per batch
   struct TbLayerMaps { CUtensorMap wqkv, wo, w13, w2; };
@@ -183,6 +183,7 @@ struct vx_handle {
   std::unordered_map<long long, G> g_batch;   // batched decode step graphs, key (slot0, n)
   void* tb_buf = nullptr;
   float *tb_h = nullptr, *tb_y = nullptr, *tb_q = nullptr, *tb_att = nullptr, *tb_part = nullptr, *tb_ws = nullptr;
+  float* tb_ar = nullptr;              // tp > 1: [tb_cap][D] partial rows of o_proj / down, all-reduced in place
   int* tb_att_tickets = nullptr;
   __half *tb_hi = nullptr, *tb_lo = nullptr;
   size_t tb_ws_floats = 0;
@@ -711,8 +712,9 @@ int run_tc_gemm(vx_handle* h, const CUtensorMap& w, const CUtensorMap& xhi, cons
 // Per-row epilogue launch (k_tb_row): split-K sum + residual + RMSNorm -> hi/lo, or
 // split-K sum + RoPE + K/V append.
 int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float* y, long long ldy, int M,
-           const __half* norm_w, const tc::RopeKvParams* rope) {
+           const __half* norm_w, const tc::RopeKvParams* rope, const float* add = nullptr) {
   tc::RowParams rp{};
+  rp.add = add;
   rp.ws = h->tb_ws; rp.splits = splits; rp.n_tiles = n_tiles; rp.bn = bn; rp.y = y; rp.ldy = ldy; rp.M = M;
   rp.mode = mode; rp.norm_w = norm_w; rp.eps = h->cfg.norm_eps; rp.hi = h->tb_hi; rp.lo = h->tb_lo;
   if (rope) rp.rope = *rope;
@@ -786,15 +788,31 @@ int tb_layers(vx_handle* h, int n, const tc::TokRows& tr, int slot0, int rows_co
     ap.n_splits = nsb; ap.scale = 1.0f / sqrtf((float)h->HD); ap.rows_consecutive = rows_consecutive;
     ap.out_hi = h->tb_hi; ap.out_lo = h->tb_lo;
     CK(launch(h, attn::k_attn_decode, dim3(h->NKV, nsb, n), dim3(attn::kThreads), attn::kSmemBytes, h->kv_map, ap));
-    if ((rc = run_tc_gemm<BN>(h, mp.wo, xh[1], xl[1], h->tb_h, D, D, n, h->QD, 1, 8, &sp))) return rc;
-    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, n_tiles, BN, h->tb_h, D, D, W.ffn_norm, nullptr))) return rc;
+    const __half* next_norm = l + 1 < h->L ? h->layers[l + 1].attn_norm : nullptr;
+    if (h->tp == 1) {
+      if ((rc = run_tc_gemm<BN>(h, mp.wo, xh[1], xl[1], h->tb_h, D, D, n, h->QD, 1, 8, &sp))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, n_tiles, BN, h->tb_h, D, D, W.ffn_norm, nullptr))) return rc;
+    } else {
+      // tensor parallelism: this rank's o_proj partial over its heads, summed over the
+      // ranks (NCCL all-reduce), then h += sum and the ffn norm
+      if ((rc = run_tc_gemm<BN>(h, mp.wo, xh[1], xl[1], h->tb_ar, D, D, n, h->QD, 0))) return rc;
+      if ((rc = allreduce_inplace(h, h->tb_ar, (size_t)n * D))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, n_tiles, BN, h->tb_h, D, D, W.ffn_norm, nullptr, h->tb_ar)))
+        return rc;
+    }
     if ((rc = run_tc_gemm<BN>(h, mp.w13, xh[0], xl[0], h->tb_y, 2LL * h->Fl, 2 * h->Fl, n, D, 0))) return rc;
     const long long ng = (long long)n * h->Fl;
     CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
               dim3(256), 0, (const float*)h->tb_y, n, h->Fl, h->tb_hi, h->tb_lo));
-    if ((rc = run_tc_gemm<BN>(h, mp.w2, xh[2], xl[2], h->tb_h, D, D, n, h->Fl, 1, 8, &sp))) return rc;
-    const __half* next_norm = l + 1 < h->L ? h->layers[l + 1].attn_norm : nullptr;
-    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, n_tiles, BN, h->tb_h, D, D, next_norm, nullptr))) return rc;
+    if (h->tp == 1) {
+      if ((rc = run_tc_gemm<BN>(h, mp.w2, xh[2], xl[2], h->tb_h, D, D, n, h->Fl, 1, 8, &sp))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, n_tiles, BN, h->tb_h, D, D, next_norm, nullptr))) return rc;
+    } else {
+      if ((rc = run_tc_gemm<BN>(h, mp.w2, xh[2], xl[2], h->tb_ar, D, D, n, h->Fl, 0))) return rc;
+      if ((rc = allreduce_inplace(h, h->tb_ar, (size_t)n * D))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, n_tiles, BN, h->tb_h, D, D, next_norm, nullptr, h->tb_ar)))
+        return rc;
+    }
   }
   return VX_OK;
 }
@@ -899,6 +917,7 @@ int setup_tb(vx_handle* h) {
   add(cap * D * 4); add(cap * ymax * 4); add(cap * h->QD * 4); add(cap * h->QD * 4);
   add(cap * h->NKV * attn::kGqa * attn::kPartStride * 4); add(h->tb_ws_floats * 4);
   add(cap * h->NKV * 4); add(cap * kmax * 2); add(cap * kmax * 2);
+  if (h->tp > 1) add(cap * D * 4);
   if (cudaMalloc(&h->tb_buf, bytes) != cudaSuccess) return h->fail(VX_E_NOMEM, "token-batch buffers (%.1f MB)", bytes / 1e6);
   CK(cudaMemset(h->tb_buf, 0, bytes));
   uint8_t* cur = (uint8_t*)h->tb_buf;
@@ -911,6 +930,7 @@ int setup_tb(vx_handle* h) {
   h->tb_att_tickets = (int*)carve(cur, cap * h->NKV * 4);
   h->tb_hi = (__half*)carve(cur, cap * kmax * 2);
   h->tb_lo = (__half*)carve(cur, cap * kmax * 2);
+  if (h->tp > 1) h->tb_ar = (float*)carve(cur, cap * D * 4);
   int rc;
   const long long ks[3] = {D, (long long)h->QD, (long long)h->Fl};
   for (int i = 0; i < 3; ++i) {
@@ -1005,6 +1025,8 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
   else if (!(c.tp_size == 1 || c.tp_size == 2 || c.tp_size == 4 || c.tp_size == 8) || c.tp_rank < 0 ||
            c.tp_rank >= c.tp_size)
     rc = bad("tp_size must be 1, 2, 4 or 8 with 0 <= tp_rank < tp_size");
+  else if (c.vocab_size < 1 || c.vocab_size % c.tp_size)
+    rc = bad("vocab_size must be a positive multiple of tp_size (the LM head is vocab-sharded)");
   else if (c.fm_nfe < 2 || c.fm_n_acoustic != 36 || c.fm_semantic_vocab < 8194 || c.audio_vocab < 9022)
     rc = bad("bad acoustic-transformer config");
   if (rc) { *out = h; return rc; }
@@ -1220,9 +1242,11 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     h->use_mk = h->coop && h->tp == 1;   // TP: enabled by vx_tp_p2p_open
   }
   {
-    h->use_tb = h->tp == 1;
-    if (h->use_tb && (rc = setup_tb(h))) { *out = h; return rc; }
-    h->fm_tc = h->use_tb && c.enable_fm;
+    // token batches on the tensor cores; under tensor parallelism their all-reduces
+    // need the NCCL communicator of vx_tp_init
+    h->use_tb = true;
+    if ((rc = setup_tb(h))) { *out = h; return rc; }
+    h->fm_tc = h->tp == 1 && c.enable_fm;   // the acoustic transformer is replicated under TP (per-op GEMVs)
   }
   *out = h;
   return VX_OK;
@@ -1259,7 +1283,7 @@ void vx_destroy(vx_handle* h) {
 int vx_selftest_gemm(vx_handle* h, int32_t M, int32_t N, int32_t K, int32_t bn, int32_t max_splits, uint64_t seed,
                      double* out_rel_err) {
   if (!h || !out_rel_err) return VX_E_INVALID;
-  if (!h->use_tb) return h->fail(VX_E_STATE, "token-batch path is off (tp > 1 or VX_NO_BATCHED_PREFILL)");
+  if (!h->use_tb) return h->fail(VX_E_STATE, "token-batch path is off");
   if (M < 1 || N < 1 || K < 64 || K % 64 || !(bn == 16 || bn == 64 || bn == 128 || bn == 256) || max_splits < 1 ||
       (long long)M * K > (1LL << 28) || (long long)N * K > (1LL << 26) || (long long)N * M > (1LL << 26))
     return h->fail(VX_E_INVALID, "selftest shape M=%d N=%d K=%d bn=%d", M, N, K, bn);
@@ -1556,7 +1580,7 @@ int vx_prefill(vx_handle* h, int32_t slot, const int32_t* tokens, int32_t n, int
   u.set_mode = 1; u.mode = kEmbPrompt; u.token = 0;
   u.set_prompt_len = 1; u.prompt_len = p0 + n;
   if ((rc = slot_update(h, slot, u))) return rc;
-  if (h->use_tb && !h->prefill_tokenwise) {
+  if (h->use_tb && !h->prefill_tokenwise && (h->tp == 1 || h->comm)) {
     if ((rc = prefill_tb(h, slot, n))) return rc;
   } else if (h->use_mk) {
     if ((rc = launch_steps(h, slot, n, kEmbPrompt, 0, kEmbPrompt, false, false))) return rc;
@@ -1573,18 +1597,37 @@ static int step_common(vx_handle* h, int slot, float* normed_out, int32_t* argma
   if ((rc = run_prog(h, kProgStep, slot))) return rc;
   h->pos_host[slot] += 1;
   if (argmax_out) {
+    // tied LM head (src/engine.ts:1017-1041); under tensor parallelism each rank scores
+    // its 1/tp of the vocabulary and a max all-reduce of 64-bit keys picks the winner
+    const int vs = h->V / h->tp, r0 = h->rank * vs;
     gemv::Params p{};
-    p.W = h->tok_emb; p.ldw = h->D; p.rows = h->V; p.col0 = 0; p.kc = h->D;
+    p.W = h->tok_emb + (size_t)r0 * h->D; p.ldw = h->D; p.rows = vs; p.col0 = 0; p.kc = h->D;
     p.x = h->normed + (size_t)slot * h->D; p.ldx = h->D; p.y = h->logits; p.ldy = 0;
     if ((rc = run_gemv<1, 6, 3, gemv::kStore, false>(h, p))) return rc;
-    CK(launch(h, k_argmax, dim3(1), dim3(1024), 0, (const float*)h->logits, h->V, h->argmax_dev));
-    CK(cudaMemcpyAsync(h->pinned, h->argmax_dev, 4, cudaMemcpyDeviceToHost, h->stream));
+    CK(launch(h, k_argmax, dim3(1), dim3(1024), 0, (const float*)h->logits, vs, h->argmax_dev));
+    if (h->tp == 1) {
+      CK(cudaMemcpyAsync(h->pinned, h->argmax_dev, 4, cudaMemcpyDeviceToHost, h->stream));
+    } else {
+      unsigned long long* key = reinterpret_cast<unsigned long long*>(h->argmax_dev + 4);
+      CK(launch(h, k_argmax_key, dim3(1), dim3(32), 0, (const float*)h->logits, (const int32_t*)h->argmax_dev, r0, key));
+      ncclResult_t r = g_nccl.allReduce(key, key, 1, ncclUint64, ncclMax, h->comm, h->stream);
+      if (r != ncclSuccess) return h->fail(VX_E_NCCL, "ncclAllReduce (LM-head argmax): %s", g_nccl.getErrorString(r));
+      CK(cudaMemcpyAsync(h->pinned, key, 8, cudaMemcpyDeviceToHost, h->stream));
+    }
   }
   if (normed_out)
     CK(cudaMemcpyAsync(h->pinned + 64, h->normed + (size_t)slot * h->D, (size_t)h->D * 4, cudaMemcpyDeviceToHost,
                        h->stream));
   if ((rc = finish(h))) return rc;
-  if (argmax_out) memcpy(argmax_out, h->pinned, 4);
+  if (argmax_out) {
+    if (h->tp == 1) {
+      memcpy(argmax_out, h->pinned, 4);
+    } else {
+      unsigned long long key;
+      memcpy(&key, h->pinned, 8);
+      *argmax_out = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+    }
+  }
   if (normed_out) memcpy(normed_out, h->pinned + 64, (size_t)h->D * 4);
   return VX_OK;
 }
@@ -1780,7 +1823,8 @@ int vx_decode_batch(vx_handle* h, int32_t slot0, int32_t n_slots, int32_t n_fram
     return h->fail(VX_E_RANGE, "slots [%d, %d) outside [0, %d)", slot0, slot0 + n_slots, h->B);
   if (n_frames < 0) return h->fail(VX_E_INVALID, "n_frames");
   if ((rc = check_slot(h, slot0))) return rc;
-  if (!h->use_tb) return h->fail(VX_E_STATE, "batched decode needs the token-batch path (tp_size 1)");
+  if (!h->use_tb) return h->fail(VX_E_STATE, "batched decode needs the token-batch path");
+  if (h->tp > 1 && !h->comm) return h->fail(VX_E_STATE, "tensor-parallel batched decode needs vx_tp_init (NCCL)");
   if (n_slots > h->tb_cap) return h->fail(VX_E_RANGE, "%d slots exceed the batch capacity %d", n_slots, h->tb_cap);
   if (n_frames == 0) return VX_OK;
   for (int s = slot0; s < slot0 + n_slots; ++s) {
@@ -1948,7 +1992,7 @@ int vx_set_option(vx_handle* h, const char* name, int64_t value) {
     h->use_mk = value != 0;
   } else if (n == "batched_prefill") {
     if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "batched_prefill must be 0 or 1");
-    if (value && !h->use_tb) return h->fail(VX_E_STATE, "batched prefill needs tp_size 1");
+    if (value && !h->use_tb) return h->fail(VX_E_STATE, "the token-batch path is off");
     h->prefill_tokenwise = value == 0;
   } else if (n == "l2_prefetch_tiles") {
     if (value < 0 || value > mk::kMaxPrefetchAhead)
