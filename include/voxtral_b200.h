@@ -225,6 +225,12 @@ int vx_synchronize(vx_handle* h);
  *   "batched_prefill"    1 (default, tp_size 1): vx_prefill runs the prompt through
  *                        tensor-core GEMMs in batches of up to 512 positions; 0: token
  *                        by token, as the reference (src/engine.ts:2457-2472).
+ *   "residual_handoff"   1 (default): the persistent kernel's o_proj / down epilogues hand
+ *                        the residual stream to the next phase as tagged 8-byte words
+ *                        that the next phase polls (a one-rank form of its tensor-parallel
+ *                        all-reduce), so that phase starts without a grid barrier; 0: the
+ *                        epilogues add into the residual and the next phase waits at a
+ *                        grid barrier (tp_size 1 only).
  *   "l2_prefetch_tiles"  0-32 (default 3): weight tiles the persistent kernel prefetches
  *                        into L2 ahead of its shared-memory ring.
  *   "wait_limit"         polls before a wait of the persistent kernel on a grid barrier
@@ -252,10 +258,12 @@ int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, dou
 
 /* Phase tracing of the persistent decode kernel (the reference records stage
  * wall-clock times only, src/engine.ts:2428-2601).  mode 1 arms tracing for the next
- * persistent launch on this handle; mode 0 copies the trace out: %globaltimer stamps
- * (ns) indexed [cta][step < 2][phase][4] = {consumers released by the grid barrier,
- * consumers done, epilogue arrival, consumers' prologue done}; mode 2 only reports the
- * dimensions.  dims (nullable) receives {ctas, steps, phases, 4}. */
+ * persistent launch on this handle; mode 0 copies the trace out, indexed
+ * [cta][step < 2][phase][8]: %globaltimer stamps (ns) {0: consumers released, 1:
+ * consumers done, 2: epilogue arrival, 3: consumers' prologue done}, then SM cycles spent
+ * waiting {4: consumer warp 0 on weight stages, 5: consumer warp 0 on reduction slots,
+ * 6: epilogue warp on reduction results}, 7 unused; mode 2 only reports the dimensions.
+ * dims (nullable) receives {ctas, steps, phases, 8}. */
 int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n_elems, int32_t* dims);
 
 /* Test support for the tensor-core GEMM of the batched paths (tcgen05 / TMEM,

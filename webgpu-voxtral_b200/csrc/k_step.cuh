@@ -95,7 +95,7 @@ struct StepParams {
   const float* rope_freq;
   SlotState* slots; int slot;
   unsigned* bar;          // grid barrier counter, zero at launch
-  unsigned long long* trace;  // nullable: [G][kTraceFrames * phases][3] globaltimer stamps
+  unsigned long long* trace;  // nullable: [G][kTraceFrames][phases][kTraceSlots] (see trace_mark)
   int prefetch_ahead;     // weight tiles prefetched into L2 ahead of the ring (0..kMaxPrefetchAhead)
   int n_frames;
   int mode0, token0;      // embedding of the first step
@@ -220,7 +220,7 @@ __device__ __forceinline__ float4 wait_tagged4(const unsigned long long* p, uint
 // synchronise inside the CTA.
 template <int N>
 __device__ __forceinline__ void grid_wait(const StepParams& p, unsigned target, int ctid, bool skip_grid = false) {
-  if (ctid == 0 && !(N > 1 && skip_grid)) {
+  if (ctid == 0 && !skip_grid) {
     const uint32_t limit = p.wait_limit ? p.wait_limit : kBarPolls;
     uint32_t i = 0;
     while (ld_relaxed(p.bar) < target) {
@@ -240,14 +240,21 @@ __device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, 
   __syncwarp();
   if (lane == 0) red_release_add(p.bar, 1u);
 }
-// Phase trace (globaltimer ns) for the first kTraceFrames steps when p.trace is set:
-// [cta][phase][0] = consumers released, [1] = consumers done, [2] = epilogue arrival,
-// [3] = consumers' x' prologue done (GEMV phases).
-constexpr int kTraceFrames = 2;
-__device__ __forceinline__ void trace_mark(const StepParams& p, int c, int f, int kl, int which, int L, int t0) {
+// Phase trace for the first kTraceFrames steps when p.trace is set, per [cta][step][phase]:
+// globaltimer stamps (ns) [0] = consumers released, [1] = consumers done, [2] = epilogue
+// arrival, [3] = consumers' x' prologue done (GEMV phases); SM cycles spent waiting
+// [4] = consumer warp 0 on weight stages, [5] = consumer warp 0 on reduction slots,
+// [6] = epilogue warp on reduction results.
+constexpr int kTraceFrames = 2, kTraceSlots = 8;
+__device__ __forceinline__ void trace_val(const StepParams& p, int c, int f, int kl, int which, int L, int t0,
+                                          unsigned long long v) {
   if (p.trace && f < kTraceFrames && t0 == 0)
-    p.trace[(((long long)c * kTraceFrames + f) * (2 + 5 * L) + kl) * 4 + which] = globaltimer();
+    p.trace[(((long long)c * kTraceFrames + f) * (2 + 5 * L) + kl) * kTraceSlots + which] = v;
 }
+__device__ __forceinline__ void trace_mark(const StepParams& p, int c, int f, int kl, int which, int L, int t0) {
+  if (p.trace && f < kTraceFrames && t0 == 0) trace_val(p, c, f, kl, which, L, t0, globaltimer());
+}
+__device__ __forceinline__ long long clk() { return clock64(); }
 
 __device__ __forceinline__ int first_tile(int c, int off, int G) { return (c - off % G + G) % G; }
 
@@ -412,7 +419,7 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
   float2 wn[CPL][2];
   float ss = 0.f;
   float4 hv[CPL];
-  if (N > 1 && ar) {
+  if (ar) {
     // all-reduce: h = h_old + partials of ranks 0..N-1, the same order on every rank
     int cols[CPL];
 #pragma unroll
@@ -432,7 +439,7 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
   for (int j = 0; j < CPL; ++j) {
     const int col = (wk + WK * j) * 128 + lane * 4;
     float4 v;
-    if (N > 1 && ar) {
+    if (ar) {
       v = hv[j];
     } else {
       v = *reinterpret_cast<const float4*>(x + col);
@@ -464,7 +471,7 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
       const int col = (wk + WK * j) * 128 + lane * 4;
-      const float4 raw = N > 1 && ar ? hv[j] : *reinterpret_cast<const float4*>(x + col);
+      const float4 raw = ar ? hv[j] : *reinterpret_cast<const float4*>(x + col);
       *reinterpret_cast<float4*>(p.dbg + (long long)rec_row * D + col) = raw;
       *reinterpret_cast<float4*>(p.dbg + (long long)(rec_row + 1) * D + col) =
           make_float4(xr[j][0], xr[j][1], xr[j][2], xr[j][3]);
@@ -474,6 +481,8 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
   const int my_idx = gemv::transpose_index<P>(lane);
   const bool writer = lane < P && my_idx < RW * TG;
   const uint32_t rowbytes = (uint32_t)kc * 2u;
+  const bool tw = p.trace && f < kTraceFrames;   // wait accounting for the trace
+  long long w_full = 0, w_red = 0;
   for (int g0 = first_tile(c, off, G); g0 < T; g0 += TG * G, ++rit) {
     float acc[TG][RW];
 #pragma unroll
@@ -484,7 +493,9 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
     for (int u = 0; u < TG; ++u) {
       if (g0 + u * G >= T) break;
       const int st = it % kStages;
+      const long long t0 = tw ? clk() : 0;
       if (!mbar_wait(&s.full[st], (it / kStages) & 1u, kDevTimeoutFull)) return false;
+      if (tw) w_full += clk() - t0;
       const uint8_t* base =
           s.ring + (size_t)st * kStageBytes + (size_t)(wk * 128 + lane * 4) * 2 + (size_t)(wr * RW) * rowbytes;
 #pragma unroll
@@ -510,11 +521,15 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
     for (int i = 0; i < P; ++i) v[i] = i < RW * TG ? acc[i / RW][i % RW] : 0.f;
     const float rv = gemv::transpose_reduce<P>(v, lane);
     const int rs = rit % kRedSlots;
+    const long long t1 = tw ? clk() : 0;
     if (!mbar_wait(&s.rempty[rs], ((rit / kRedSlots) & 1u) ^ 1u, kDevTimeoutRed)) return false;
+    if (tw) w_red += clk() - t1;
     if (writer) s.red[(rs * kCW + cw) * kMaxVals + my_idx] = rv;
     __syncwarp();
     if (lane == 0) mbar_arrive(&s.rfull[rs]);
   }
+  trace_val(p, c, f, kl, 4, p.n_layers, cw * 32 + lane, (unsigned long long)w_full);
+  trace_val(p, c, f, kl, 5, p.n_layers, cw * 32 + lane, (unsigned long long)w_red);
   return true;
 }
 
@@ -526,8 +541,10 @@ __device__ __forceinline__ bool consume(const StepParams& p, Smem& s, uint32_t& 
 constexpr int kPeer = 100;
 template <int R, int EPI, int TG, int WK = kCW, int N = 1>
 __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t& rit, float* y, int rows, int T,
-                                         int off, int c, int G, int lane, int layer, int pos,
+                                         int off, int c, int G, int lane, int layer, int pos, int f, int kl,
                                          unsigned long long ar_k = 0) {
+  const bool tw = p.trace && f < kTraceFrames;
+  long long w_red = 0;
   using TD = Tp<N>;
   constexpr int ORT = EPI == gemv::kSwiglu ? R / 2 : R;
   constexpr int RW = R / (kCW / WK);
@@ -542,7 +559,9 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
       const int row = t * ORT + r;
       if (live && row < rows) yold = y[row];
     }
+    const long long t0 = tw ? clk() : 0;
     if (!mbar_wait(&s.rfull[rs], (rit / kRedSlots) & 1u, kDevTimeoutRed)) return false;
+    if (tw) w_red += clk() - t0;
     float val = 0.f;
     if (lane < R * TG) {
       // row r of tile u: written by the WK warps of row group r / RW at index u*RW + r%RW
@@ -596,6 +615,7 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
       }
     }
   }
+  trace_val(p, c, f, kl, 6, p.n_layers, lane, (unsigned long long)w_red);
   grid_arrive_warp<N>(p, lane, EPI == gemv::kQkv);
   return true;
 }
@@ -866,9 +886,14 @@ __device__ __forceinline__ int embed_source(const StepParams& p, int mode, int t
 }
 
 // ---------------------------------------------------------------- the kernel
-template <int N>
+// AR: the residual stream is handed from the o_proj / down epilogues to the next phase
+// as tagged words (the all-reduce protocol above; with N = 1 a one-source all-reduce),
+// so the phase after each residual update starts without a grid barrier.  !AR (N = 1
+// only): the epilogues add into h and the next phase waits at a grid barrier.
+template <int N, bool AR>
 __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_constant__ CUtensorMap kvmap,
                                                               const __grid_constant__ StepParams p) {
+  static_assert(AR || N == 1, "tensor parallelism hands the residual over as tagged words");
   using TD = Tp<N>;
   extern __shared__ uint8_t smem_raw[];
   Smem s = smem_map(smem_raw);
@@ -894,7 +919,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       Cursor cur, ahead;
       cursor_start<N>(p, cur, c, G, L);
       cursor_start<N>(p, ahead, c, G, L);
-      for (int i = 0; i < p.prefetch_ahead && ahead.f < p.n_frames; ++i) {
+      int dist = 0;   // tiles the L2 lookahead runs ahead of the ring
+      for (; dist < p.prefetch_ahead && ahead.f < p.n_frames; ++dist) {
         const __half *a, *b; uint32_t bytes; int ort;
         tile_src<N>(p, ahead, a, b, bytes, ort);
         prefetch_l2(a, bytes);
@@ -912,11 +938,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         if (b) bulk_g2s(dst + (size_t)ort * D * 2, b, bytes, &s.full[st], pol);   // SwiGLU up rows after the gate rows
         ++it;
         cursor_next<N>(p, cur, c, G, L);
-        if (p.prefetch_ahead > 0 && ahead.f < p.n_frames) {
+        if (dist > 0) --dist;
+        while (dist < p.prefetch_ahead && ahead.f < p.n_frames) {
           tile_src<N>(p, ahead, a, b, bytes, ort);
           prefetch_l2(a, bytes);
           if (b) prefetch_l2(b, bytes);
           cursor_next<N>(p, ahead, c, G, L);
+          ++dist;
         }
       }
       // drain the copies still in flight
@@ -941,22 +969,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         const int o3 = (int)((tiles_before + TD::TQKV + TD::TO + TD::TW13) % G);
         const int kl = 1 + 5 * l;
         const unsigned long long k_o = kf + 2 * l, k_w2 = kf + 2 * l + 1;
-        if (!epilogue<6, gemv::kQkv, kTgQKV, kCW, N>(p, s, rit, nullptr, TD::QKVD, TD::TQKV, o0, c, G, lane, l, pos))
+        if (!epilogue<6, gemv::kQkv, kTgQKV, kCW, N>(p, s, rit, nullptr, TD::QKVD, TD::TQKV, o0, c, G, lane, l, pos, f, kl))
           return;
         trace_mark(p, c, f, kl, 2, L, lane);
-        if constexpr (N == 1) {
-          if (!epilogue<4, gemv::kResid, kTgO>(p, s, rit, p.h, D, TD::TO, o1, c, G, lane, l, pos)) return;
+        if constexpr (!AR) {
+          if (!epilogue<4, gemv::kResid, kTgO>(p, s, rit, p.h, D, TD::TO, o1, c, G, lane, l, pos, f, kl + 2)) return;
         } else {
-          if (!epilogue<TD::RO, kPeer, 1, TD::WKO, N>(p, s, rit, nullptr, D, TD::TO, o1, c, G, lane, l, pos, k_o))
+          if (!epilogue<TD::RO, kPeer, 1, TD::WKO, N>(p, s, rit, nullptr, D, TD::TO, o1, c, G, lane, l, pos, f, kl + 2, k_o))
             return;
         }
         trace_mark(p, c, f, kl + 2, 2, L, lane);
-        if (!epilogue<6, gemv::kSwiglu, kTgW13, kCW, N>(p, s, rit, p.g, TD::F, TD::TW13, o2, c, G, lane, l, pos)) return;
+        if (!epilogue<6, gemv::kSwiglu, kTgW13, kCW, N>(p, s, rit, p.g, TD::F, TD::TW13, o2, c, G, lane, l, pos, f, kl + 3)) return;
         trace_mark(p, c, f, kl + 3, 2, L, lane);
-        if constexpr (N == 1) {
-          if (!epilogue<2, gemv::kResid, kTgW2>(p, s, rit, p.h, D, TD::TW2, o3, c, G, lane, l, pos)) return;
+        if constexpr (!AR) {
+          if (!epilogue<2, gemv::kResid, kTgW2>(p, s, rit, p.h, D, TD::TW2, o3, c, G, lane, l, pos, f, kl + 4)) return;
         } else {
-          if (!epilogue<TD::RW2, kPeer, 1, TD::WKW2, N>(p, s, rit, nullptr, D, TD::TW2, o3, c, G, lane, l, pos, k_w2))
+          if (!epilogue<TD::RW2, kPeer, 1, TD::WKW2, N>(p, s, rit, nullptr, D, TD::TW2, o3, c, G, lane, l, pos, f, kl + 4, k_w2))
             return;
         }
         trace_mark(p, c, f, kl + 4, 2, L, lane);
@@ -979,7 +1007,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   // (all-reduce k reads h[k & 1] and its parity k & 1 of the receive buffer, writes
   // h[(k + 1) & 1]); every launch starts at an even all-reduce index, so EMBED
   // writes p.h and the last all-reduce of a launch leaves the residual in p.h.
-  float* const hb[2] = {p.h, N > 1 ? p.h2 : p.h};
+  float* const hb[2] = {p.h, AR ? p.h2 : p.h};
   auto ar_in = [&](unsigned long long k) {
     return ArIn{hb[k & 1], p.recv + (long long)(k & 1) * N * D, hb[(k + 1) & 1], (uint32_t)(k + 1),
                 p.hx + (long long)(k & 1) * D, e0, e1, p.wait_limit ? p.wait_limit : kTagPolls};
@@ -1040,7 +1068,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       const int kl = 1 + 5 * l;
       const unsigned long long k_o = kf + 2 * l, k_prev = kf + 2 * l - 1;   // k_prev: layer l-1's down
       // ---- QKV (+ RoPE + KV append in the epilogue warp); TP: h = all-reduce of layer l-1's down
-      const bool ar_qkv = N > 1 && l > 0;
+      const bool ar_qkv = AR && l > 0;
       grid_wait<N>(p, phase * G, ctid, ar_qkv);
       trace_mark(p, c, f, kl, 0, L, ctid);
       prefetch_kv<N>(p, l, pos, c, G, ctid);
@@ -1066,12 +1094,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       trace_mark(p, c, f, kl + 2, 1, L, ctid);
       ++phase;
       // ---- gate/up + SwiGLU; TP: h = all-reduce of o_proj
-      grid_wait<N>(p, phase * G, ctid, true);
+      grid_wait<N>(p, phase * G, ctid, AR);
       trace_mark(p, c, f, kl + 3, 0, L, ctid);
       {
-        const ArIn a = N > 1 ? ar_in(k_o) : ArIn{};
+        const ArIn a = AR ? ar_in(k_o) : ArIn{};
         consume<6, 3, true, kTgW13, kCW, N>(p, s, it, rit, hb[0], W.ffn_norm, D, TD::TW13, o2, c, G, cw, lane, pos, f,
-                                            kl + 3, N > 1 ? &a : nullptr, 4 * l + 2);
+                                            kl + 3, AR ? &a : nullptr, 4 * l + 2);
       }
       trace_mark(p, c, f, kl + 3, 1, L, ctid);
       ++phase;
@@ -1087,17 +1115,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     // ---- FINAL norm (each CTA: full sum of squares, its slice of the output);
     // TP: h = all-reduce of the last layer's down (CTA 0 stores it to p.h)
     const unsigned long long k_last = kf + 2ull * L - 1;
-    grid_wait<N>(p, phase * G, ctid, true);
+    grid_wait<N>(p, phase * G, ctid, AR);
     trace_mark(p, c, f, 1 + 5 * L, 0, L, ctid);
     {
-      const ArIn fa = N > 1 ? ar_in(k_last) : ArIn{};
+      const ArIn fa = AR ? ar_in(k_last) : ArIn{};
       // TP, two stages: stage A leaves this CTA's slice in fa.h_new (= p.h), written by
       // the same threads that read it back in the slice pass below.  One stage: the
       // summed row is staged in the (idle) attention buffer for the slice pass.
       float* hs = reinterpret_cast<float*>(s.attn);
-      auto hval = [&](int i) -> float { return N == 1 ? p.h[i] : kArTwoStage<N> ? fa.h_new[i] : hs[i]; };
+      auto hval = [&](int i) -> float { return !AR ? p.h[i] : kArTwoStage<N> ? fa.h_new[i] : hs[i]; };
       float ss = 0.f;
-      if constexpr (N == 1) {
+      if constexpr (!AR) {
         for (int i = ctid; i < D; i += kCW * 32) ss += p.h[i] * p.h[i];
       } else {
         constexpr int U = D / (kCW * 32 * 4);

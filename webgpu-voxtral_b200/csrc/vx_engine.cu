@@ -167,6 +167,7 @@ struct vx_handle {
   int prefetch_ahead = 3;   // persistent kernel: L2 lookahead in weight tiles (option l2_prefetch_tiles; measured best)
   uint32_t wait_limit = 0;  // persistent kernel: polls before a barrier / peer wait gives up (option wait_limit; 0 = built-in)
   bool tp_loopback = false; // option tp_loopback: every peer receive buffer is this handle's own (test support)
+  bool tagged = true;       // tp 1: residual handed over as tagged words (option residual_handoff)
   bool trace_armed = false;
 
   // token batches on the tensor cores (k_gemm.cuh): batched prefill
@@ -255,10 +256,11 @@ int prime_kernel_attrs(vx_handle* h) {
   CK(gemv_attr<6, 4, 3, kSwiglu, true>()); CK(gemv_attr<6, 4, 3, kResid, false>());
   CK(gemv_attr<2, 6, 3, kStore, true>());
   CK(cudaFuncSetAttribute(attn::k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn::kSmemBytes));
-  CK(cudaFuncSetAttribute(mk::k_decode_steps<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
-  CK(cudaFuncSetAttribute(mk::k_decode_steps<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
-  CK(cudaFuncSetAttribute(mk::k_decode_steps<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
-  CK(cudaFuncSetAttribute(mk::k_decode_steps<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
+  CK(cudaFuncSetAttribute(mk::k_decode_steps<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::kSmemBytes));
   CK(cudaFuncSetAttribute(k_fm_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem));
   CK(cudaFuncSetAttribute(k_top_p_test, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSampleSmem));
   CK(tc_attr<16>()); CK(tc_attr<64>()); CK(tc_attr<128>()); CK(tc_attr<256>());
@@ -308,7 +310,8 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  if (h->tp > 1) {
+  const bool ar = h->tp > 1 || h->tagged;
+  if (ar) {
     if (!h->p2p_ready) return h->fail(VX_E_STATE, "tensor-parallel persistent kernel needs vx_tp_p2p_open");
     sp.rank = h->rank;
     sp.h2 = h->h2 + slot * D;
@@ -319,12 +322,15 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
   }
   h->launches++;
   switch (h->tp) {
-    case 1: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<1>, h->kv_map, sp)); break;
-    case 2: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<2>, h->kv_map, sp)); break;
-    case 4: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<4>, h->kv_map, sp)); break;
-    default: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<8>, h->kv_map, sp)); break;
+    case 1:
+      if (ar) CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<1, true>, h->kv_map, sp));
+      else CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<1, false>, h->kv_map, sp));
+      break;
+    case 2: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<2, true>, h->kv_map, sp)); break;
+    case 4: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<4, true>, h->kv_map, sp)); break;
+    default: CK(cudaLaunchKernelEx(&cfg, mk::k_decode_steps<8, true>, h->kv_map, sp)); break;
   }
-  if (h->tp > 1) h->ar_base += 2ull * h->L * (unsigned long long)n_frames;
+  if (ar) h->ar_base += 2ull * h->L * (unsigned long long)n_frames;
   return VX_OK;
 }
 
@@ -1240,6 +1246,14 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->dev);
     h->coop = coop != 0;
     h->use_mk = h->coop && h->tp == 1;   // TP: enabled by vx_tp_p2p_open
+    if (h->coop && h->tp == 1) {
+      // the persistent kernel's tagged residual words (a one-rank all-reduce)
+      if (cudaMalloc(&h->p2p_buf, kP2pBytes) != cudaSuccess || cudaMemset(h->p2p_buf, 0, kP2pBytes) != cudaSuccess) {
+        *out = h; return h->fail(VX_E_NOMEM, "tagged residual words");
+      }
+      h->p2p_peer[0] = h->p2p_buf;
+      h->p2p_ready = true;
+    }
   }
   {
     // token batches on the tensor cores; under tensor parallelism their all-reduces
@@ -1967,9 +1981,9 @@ int vx_profile_step(vx_handle* h, int32_t slot, int32_t reps, float* out_ms, dou
 int vx_trace(vx_handle* h, int32_t mode, uint64_t* out, size_t n, int32_t* dims) {
   if (!h) return VX_E_INVALID;
   CK(cudaSetDevice(h->dev));
-  const size_t per = (size_t)mk::kTraceFrames * (2 + 5 * h->L) * 4;
+  const size_t per = (size_t)mk::kTraceFrames * (2 + 5 * h->L) * mk::kTraceSlots;
   const size_t total = per * h->num_sms;
-  if (dims) { dims[0] = h->num_sms; dims[1] = mk::kTraceFrames; dims[2] = 2 + 5 * h->L; dims[3] = 4; }
+  if (dims) { dims[0] = h->num_sms; dims[1] = mk::kTraceFrames; dims[2] = 2 + 5 * h->L; dims[3] = mk::kTraceSlots; }
   if (mode == 2) return VX_OK;   // dimensions only
   if (mode == 1) {
     if (!h->d_trace && cudaMalloc((void**)&h->d_trace, total * 8) != cudaSuccess) return h->fail(VX_E_NOMEM, "trace");
@@ -1990,6 +2004,10 @@ int vx_set_option(vx_handle* h, const char* name, int64_t value) {
     if (value && !h->coop) return h->fail(VX_E_STATE, "the device has no cooperative launch");
     if (value && h->tp > 1 && !h->p2p_ready) return h->fail(VX_E_STATE, "tensor parallelism: call vx_tp_p2p_open first");
     h->use_mk = value != 0;
+  } else if (n == "residual_handoff") {
+    if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "residual_handoff must be 0 or 1");
+    if (h->tp > 1 && value == 0) return h->fail(VX_E_STATE, "tensor parallelism needs residual_handoff 1");
+    h->tagged = value != 0;
   } else if (n == "batched_prefill") {
     if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "batched_prefill must be 0 or 1");
     if (value && !h->use_tb) return h->fail(VX_E_STATE, "the token-batch path is off");

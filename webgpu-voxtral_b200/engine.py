@@ -369,7 +369,8 @@ class VoxtralEngine:
         self._check(load_library().vx_trace(self._h, 1, None, 0, None))
 
     def trace_read(self) -> np.ndarray:
-        """[cta, step, phase, {released, consumers done, epilogue arrival}] in ns (0 = not recorded)."""
+        """[cta, step, phase, 8]: {released, consumers done, epilogue arrival, prologue done} in ns, then
+        SM cycles waiting {consumer warp 0 on stages, on reduction slots, epilogue on results} (0 = not recorded)."""
         L = load_library()
         dims = np.zeros(4, np.int32)
         self._check(L.vx_trace(self._h, 2, None, 0, _p(dims, _i32p)))
