@@ -70,6 +70,9 @@ def parse():
     ap.add_argument("--c5-context", type=int, default=32768, help="synthetic K/V positions per utterance (C5)")
     ap.add_argument("--c5-frames", type=int, default=256, help="frames of the long-context (C5) run; 0 = skip")
     ap.add_argument("--codec-frames", type=int, default=500, help="frames of the codec-decoder run; 0 = skip")
+    ap.add_argument("--trace", action="store_true",
+                    help="instead of the bench line: per-phase time breakdown of the persistent decode kernel "
+                         "(vx_trace) on the C2 shape at the step's mean position, one JSON line")
     return ap.parse_args()
 
 
@@ -575,10 +578,71 @@ def run_b200(args):
     return 0
 
 
+def run_trace(args):
+    """Phase breakdown of k_decode_steps (one GPU): frames/s at the step's mean position, then
+    the per-phase spans, hand-off gaps and consumer waits of the second traced step."""
+    import torch
+    vx = importlib.import_module("webgpu-voxtral_b200")
+    L = args.layers
+    pos = mean_position(args)
+    eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": L}}, "maxSeqLen": 4096, "maxFrames": 1024,
+                            "enableFM": False, "enableCodec": False})
+    eng.init()
+    eng.loadRandomWeights(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    eng.set_stream(stream.cuda_stream)
+    eng.set_streams(3, 4, 0)
+    eng.fill_kv(pos, seed=5)
+    eng.checkpoint()
+    ms = []
+    for i in range(4):
+        eng.rewind()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        eng.decode(100, with_fm=False)
+        b.record(stream)
+        torch.cuda.synchronize()
+        if i:
+            ms.append(a.elapsed_time(b) / 100)
+    eng.rewind()
+    eng.trace_arm()
+    eng.decode(4, with_fm=False)
+    eng.synchronize()
+    tr = eng.trace_read().astype(np.int64)[:, 1]   # [cta, phase, slot] of the second step
+    eng.destroy()
+    t0 = tr[:, 0, 0].min()
+    rel, done, arr, pro = (tr[:, :, i] - t0 for i in range(4))
+    names = ["qkv", "attention", "o_proj", "gate_up", "down"]
+    mhz = float(os.environ.get("SM_MHZ", "1965"))
+    phases = {}
+    for j, nm in enumerate(names):
+        ks = [1 + 5 * l + j for l in range(L)]
+        span = np.mean([np.median(rel[:, k + 1]) - np.median(rel[:, k]) for k in ks]) / 1e3
+        d = {"span_us": span,
+             "consumers_median_us": np.mean([np.median(done[:, k] - rel[:, k]) for k in ks]) / 1e3,
+             "consumers_max_us": np.mean([np.max(done[:, k] - rel[:, k]) for k in ks]) / 1e3}
+        if nm != "attention":
+            d["prologue_us"] = np.mean([np.median(pro[:, k] - rel[:, k]) for k in ks]) / 1e3
+            d["epilogue_lag_us"] = np.mean([arr[:, k].max() - done[:, k].max() for k in ks]) / 1e3
+            d["stage_wait_us"] = np.mean([np.median(tr[:, k, 4]) for k in ks]) / mhz
+            d["reduction_slot_wait_us"] = np.mean([np.median(tr[:, k, 5]) for k in ks]) / mhz
+        phases[nm] = {k: round(float(v), 3) for k, v in d.items()}
+    step_us = (np.median(rel[:, -1]) - np.median(rel[:, 0])) / 1e3
+    print(json.dumps({"trace": "k_decode_steps phase breakdown", "layers": L, "position": pos,
+                      "ms_per_frame": min(ms), "traced_step_us": float(step_us), "us_per_layer": float(step_us / L),
+                      "phases": phases, "note": "spans: median release to the next phase's median release; "
+                      "waits converted from SM cycles at SM_MHZ (default 1965)"}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.trace:
+        return run_trace(args)
     return run_b200(args)
 
 
