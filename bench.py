@@ -583,11 +583,20 @@ def run_trace(args):
     the per-phase spans, hand-off gaps and consumer waits of the second traced step."""
     import torch
     vx = importlib.import_module("webgpu-voxtral_b200")
+    vdist = importlib.import_module("webgpu-voxtral_b200.dist")
+    rank, local, world = vdist.env_rank()
+    torch.cuda.set_device(local)
+    vdist.init(timeout_s=300)
     L = args.layers
     pos = mean_position(args)
     eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": L}}, "maxSeqLen": 4096, "maxFrames": 1024,
-                            "enableFM": False, "enableCodec": False})
+                            "enableFM": False, "enableCodec": False, "device": local, "tpSize": world,
+                            "tpRank": rank})
     eng.init()
+    if world > 1:
+        lib = nccl_lib_path()
+        uid = vdist.broadcast_bytes(vx.nccl_unique_id(lib) if rank == 0 else None)
+        vx.tp_init(eng, uid, lib)
     eng.loadRandomWeights(0)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
@@ -599,19 +608,24 @@ def run_trace(args):
     for i in range(4):
         eng.rewind()
         torch.cuda.synchronize()
+        vdist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         eng.decode(100, with_fm=False)
         b.record(stream)
         torch.cuda.synchronize()
         if i:
-            ms.append(a.elapsed_time(b) / 100)
+            ms.append(vdist.max_over_ranks(a.elapsed_time(b) / 100))
     eng.rewind()
     eng.trace_arm()
     eng.decode(4, with_fm=False)
     eng.synchronize()
     tr = eng.trace_read().astype(np.int64)[:, 1]   # [cta, phase, slot] of the second step
     eng.destroy()
+    vdist.barrier()
+    vdist.shutdown()
+    if rank != 0:
+        return 0
     t0 = tr[:, 0, 0].min()
     rel, done, arr, pro = (tr[:, :, i] - t0 for i in range(4))
     names = ["qkv", "attention", "o_proj", "gate_up", "down"]
@@ -630,7 +644,7 @@ def run_trace(args):
             d["reduction_slot_wait_us"] = np.mean([np.median(tr[:, k, 5]) for k in ks]) / mhz
         phases[nm] = {k: round(float(v), 3) for k, v in d.items()}
     step_us = (np.median(rel[:, -1]) - np.median(rel[:, 0])) / 1e3
-    print(json.dumps({"trace": "k_decode_steps phase breakdown", "layers": L, "position": pos,
+    print(json.dumps({"trace": "k_decode_steps phase breakdown", "layers": L, "position": pos, "tp": world,
                       "ms_per_frame": min(ms), "traced_step_us": float(step_us), "us_per_layer": float(step_us / L),
                       "phases": phases, "note": "spans: median release to the next phase's median release; "
                       "waits converted from SM cycles at SM_MHZ (default 1965)"}), flush=True)

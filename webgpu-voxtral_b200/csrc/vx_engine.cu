@@ -176,8 +176,7 @@ struct vx_handle {
   int tb_cap = 0;                      // rows per batch
   struct TbLayerMaps { CUtensorMap wqkv, wo, w13, w2; };
   std::vector<TbLayerMaps> tb_wmaps;   // per backbone layer
-  std::vector<TbLayerMaps> fm_wmaps;   // per acoustic-transformer layer (fm_tc)
-  bool fm_tc = false;                  // acoustic transformer on the tensor-core GEMM (tp 1; per-op GEMVs otherwise)
+  std::vector<TbLayerMaps> fm_wmaps;   // per acoustic-transformer layer (its 6 sequence rows on the tensor cores)
   CUtensorMap tb_xhi[3], tb_xlo[3];    // operand pair for K = D, QD, Fl (128-row boxes)
   CUtensorMap tb_xhi64[3], tb_xlo64[3];  // the same with 64-row boxes (batches of <= 64 rows)
   CUtensorMap tb_xhi16[3], tb_xlo16[3];  // and 16-row boxes (the acoustic transformer's 6 rows)
@@ -533,7 +532,7 @@ FmParams fm_params(vx_handle* h, int slot) {
   f.seq = h->fm_seq + (long long)slot * 6 * D;
   f.qkv = h->fm_qkv + (long long)slot * 6 * (4096 + 2048);
   f.att = h->fm_att + (long long)slot * 6 * 4096;
-  f.q_dim = 4096; f.kv_dim = 1024; f.n_heads = 32; f.n_kv = 8;
+  f.q_dim = h->QD; f.kv_dim = h->KVD; f.n_heads = h->NH; f.n_kv = h->NKV;   // this rank's heads
   f.vel = h->fm_vel + (long long)slot * 72;
   f.alpha = h->cfg.fm_cfg_alpha; f.dt = (float)(1.0 / (h->cfg.fm_nfe - 1));
   f.code_ring = h->code_ring;
@@ -543,10 +542,12 @@ FmParams fm_params(vx_handle* h, int slot) {
 
 int enqueue_fm_layers_tc(vx_handle* h, const FmParams& f);
 
-// fmForward for one slot on its normed state (the FM is not sharded under TP:
-// every rank computes it redundantly).
+// fmForward for one slot on its normed state.  Under tensor parallelism the acoustic
+// transformer's heads and FFN columns are sharded like the backbone's, with an NCCL
+// all-reduce of the 6 sequence rows after o_proj and after down; the heads around it
+// (semantic head, input projection, acoustic head, Euler step) are replicated.
 int enqueue_fm(vx_handle* h, int slot) {
-  const int D = h->D, F = h->cfg.hidden_dim;
+  const int D = h->D;
   int rc;
   {  // semantic head + llm projection in one weight stream ([8320 + 3072] rows)
     gemv::Params p{};
@@ -561,37 +562,8 @@ int enqueue_fm(vx_handle* h, int slot) {
   for (int s = 0; s < steps; ++s) {
     f.step = s;
     CK(launch(h, k_fm_assemble, dim3((D + 255) / 256), dim3(256), 0, f));
-    if (h->fm_tc) {
-      if ((rc = enqueue_fm_layers_tc(h, f))) return rc;
-    } else
-    for (int l = 0; l < h->cfg.fm_n_layers; ++l) {
-      const LayerW& W = h->fm_layers[l];
-      {
-        gemv::Params p{};
-        p.W = W.wqkv; p.ldw = D; p.rows = 6144; p.col0 = 0; p.kc = D; p.x = f.seq; p.ldx = D;
-        p.norm_w = W.attn_norm; p.eps = 1e-5f; p.norm_dim = D; p.y = const_cast<float*>(f.qkv); p.ldy = 6144;
-        if ((rc = run_gemv<6, 4, 3, gemv::kStore, true>(h, p))) return rc;
-      }
-      CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, f));
-      {
-        gemv::Params p{};
-        p.W = W.wo; p.ldw = 4096; p.rows = D; p.col0 = 0; p.kc = 4096; p.x = f.att; p.ldx = 4096; p.y = f.seq; p.ldy = D;
-        if ((rc = run_gemv<6, 4, 4, gemv::kResid, false>(h, p))) return rc;
-      }
-      {
-        gemv::Params p{};
-        p.W = W.w13; p.ldw = D; p.second_off = (long long)F * D; p.rows = F; p.col0 = 0; p.kc = D;
-        p.x = f.seq; p.ldx = D; p.norm_w = W.ffn_norm; p.eps = 1e-5f; p.norm_dim = D;
-        p.y = h->fm_g + (long long)slot * 6 * F; p.ldy = F;
-        if ((rc = run_gemv<6, 4, 3, gemv::kSwiglu, true>(h, p))) return rc;
-      }
-      for (int c = 0; c < F / 3072; ++c) {
-        gemv::Params p{};
-        p.W = W.w2; p.ldw = F; p.rows = D; p.col0 = c * 3072; p.kc = 3072;
-        p.x = h->fm_g + (long long)slot * 6 * F; p.ldx = F; p.y = f.seq; p.ldy = D;
-        if ((rc = run_gemv<6, 4, 3, gemv::kResid, false>(h, p))) return rc;
-      }
-    }
+    if (h->tp > 1 && !h->comm) return h->fail(VX_E_STATE, "tensor-parallel acoustic transformer needs vx_tp_init (NCCL)");
+    if ((rc = enqueue_fm_layers_tc(h, f))) return rc;
     {  // final norm of position 0 of both sequences + acoustic_codebook_output
       gemv::Params p{};
       p.W = h->fm_ac; p.ldw = D; p.rows = 36; p.col0 = 0; p.kc = D; p.x = f.seq; p.ldx = 3LL * D;
@@ -739,27 +711,42 @@ int tb_row(vx_handle* h, int n, int mode, int splits, int n_tiles, int bn, float
 // of 6 through tcgen05 GEMMs (16-row tiles, 9-stage weight pipeline), with the pre-norms, residual adds and split-K
 // sums in k_tb_row, SwiGLU in k_tb_swiglu_split and the 3-token attention in k_fm_attn3.
 int enqueue_fm_layers_tc(vx_handle* h, const FmParams& f) {
-  const int D = h->D, F = h->cfg.hidden_dim, n = 6;
+  const int D = h->D, n = 6;
   int rc, sp = 0;
   if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 1, 16, f.seq, D, D, h->fm_layers[0].attn_norm, nullptr))) return rc;
   for (int l = 0; l < h->FL; ++l) {
     const LayerW& W = h->fm_layers[l];
     const vx_handle::TbLayerMaps& m = h->fm_wmaps[l];
-    if ((rc = run_tc_gemm<16>(h, m.wqkv, h->tb_xhi16[0], h->tb_xlo16[0], const_cast<float*>(f.qkv), 6144, 6144, n, D, 0)))
+    const __half* next = l + 1 < h->FL ? h->fm_layers[l + 1].attn_norm : nullptr;
+    if ((rc = run_tc_gemm<16>(h, m.wqkv, h->tb_xhi16[0], h->tb_xlo16[0], const_cast<float*>(f.qkv), h->QKVD, h->QKVD, n,
+                              D, 0)))
       return rc;
     FmParams fa = f;   // attention output straight into the o_proj operand
     fa.att_hi = h->tb_hi;
     fa.att_lo = h->tb_lo;
-    CK(launch(h, k_fm_attn3, dim3(16), dim3(128), 0, fa));
-    if ((rc = run_tc_gemm<16>(h, m.wo, h->tb_xhi16[1], h->tb_xlo16[1], f.seq, D, D, n, 4096, 1, 8, &sp))) return rc;
-    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, W.ffn_norm, nullptr))) return rc;
-    if ((rc = run_tc_gemm<16>(h, m.w13, h->tb_xhi16[0], h->tb_xlo16[0], h->tb_y, 2 * F, 2 * F, n, D, 0))) return rc;
-    const long long ng = (long long)n * F;
+    CK(launch(h, k_fm_attn3, dim3(2 * h->NH / 4), dim3(128), 0, fa));   // (sequence, head) per warp
+    if (h->tp == 1) {
+      if ((rc = run_tc_gemm<16>(h, m.wo, h->tb_xhi16[1], h->tb_xlo16[1], f.seq, D, D, n, h->QD, 1, 8, &sp))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, W.ffn_norm, nullptr))) return rc;
+    } else {
+      // this rank's heads: o_proj partial, summed over the ranks (NCCL), then the residual + ffn norm
+      if ((rc = run_tc_gemm<16>(h, m.wo, h->tb_xhi16[1], h->tb_xlo16[1], h->tb_ar, D, D, n, h->QD, 0))) return rc;
+      if ((rc = allreduce_inplace(h, h->tb_ar, (size_t)n * D))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 1, 16, f.seq, D, D, W.ffn_norm, nullptr, h->tb_ar))) return rc;
+    }
+    if ((rc = run_tc_gemm<16>(h, m.w13, h->tb_xhi16[0], h->tb_xlo16[0], h->tb_y, 2LL * h->Fl, 2 * h->Fl, n, D, 0)))
+      return rc;
+    const long long ng = (long long)n * h->Fl;
     CK(launch(h, tc::k_tb_swiglu_split, dim3((unsigned)std::min<long long>((ng + 255) / 256, 8L * h->num_sms)),
-              dim3(256), 0, (const float*)h->tb_y, n, F, h->tb_hi, h->tb_lo));
-    if ((rc = run_tc_gemm<16>(h, m.w2, h->tb_xhi16[2], h->tb_xlo16[2], f.seq, D, D, n, F, 1, 8, &sp))) return rc;
-    const __half* next = l + 1 < h->FL ? h->fm_layers[l + 1].attn_norm : nullptr;
-    if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, next, nullptr))) return rc;
+              dim3(256), 0, (const float*)h->tb_y, n, h->Fl, h->tb_hi, h->tb_lo));
+    if (h->tp == 1) {
+      if ((rc = run_tc_gemm<16>(h, m.w2, h->tb_xhi16[2], h->tb_xlo16[2], f.seq, D, D, n, h->Fl, 1, 8, &sp))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, sp, 1, 16, f.seq, D, D, next, nullptr))) return rc;
+    } else {
+      if ((rc = run_tc_gemm<16>(h, m.w2, h->tb_xhi16[2], h->tb_xlo16[2], h->tb_ar, D, D, n, h->Fl, 0))) return rc;
+      if ((rc = allreduce_inplace(h, h->tb_ar, (size_t)n * D))) return rc;
+      if ((rc = tb_row(h, n, tc::kRowResidNorm, 0, 1, 16, f.seq, D, D, next, nullptr, h->tb_ar))) return rc;
+    }
   }
   return VX_OK;
 }
@@ -956,16 +943,15 @@ int setup_tb(vx_handle* h) {
     if ((rc = encode_f16_2d(h, &m.w13, W.w13, D, 2LL * h->Fl, D * 2, tc::kBK, tc::kBM))) return rc;
     if ((rc = encode_f16_2d(h, &m.w2, W.w2, h->Fl, D, (long long)h->Fl * 2, tc::kBK, tc::kBM))) return rc;
   }
-  // acoustic transformer (full, unsharded weights: this path runs at tp 1 only)
+  // acoustic transformer (this rank's shard, the backbone's shapes)
   h->fm_wmaps.resize(h->FL);
   for (int l = 0; l < h->FL; ++l) {
     const LayerW& W = h->fm_layers[l];
     vx_handle::TbLayerMaps& m = h->fm_wmaps[l];
-    const long long F = h->cfg.hidden_dim;
-    if ((rc = encode_f16_2d(h, &m.wqkv, W.wqkv, D, 6144, D * 2, tc::kBK, tc::kBM))) return rc;
-    if ((rc = encode_f16_2d(h, &m.wo, W.wo, 4096, D, 4096 * 2, tc::kBK, tc::kBM))) return rc;
-    if ((rc = encode_f16_2d(h, &m.w13, W.w13, D, 2 * F, D * 2, tc::kBK, tc::kBM))) return rc;
-    if ((rc = encode_f16_2d(h, &m.w2, W.w2, F, D, F * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.wqkv, W.wqkv, D, h->QKVD, D * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.wo, W.wo, h->QD, D, h->QD * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.w13, W.w13, D, 2LL * h->Fl, D * 2, tc::kBK, tc::kBM))) return rc;
+    if ((rc = encode_f16_2d(h, &m.w2, W.w2, h->Fl, D, (long long)h->Fl * 2, tc::kBK, tc::kBM))) return rc;
   }
   return VX_OK;
 }
@@ -1059,7 +1045,8 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
 
   // ---------------------------------------------------------- weight arena
   const size_t layer_elems = (size_t)h->QKVD * D + D * (size_t)h->QD + 2 * (size_t)h->Fl * D + D * (size_t)h->Fl + 2 * D;
-  const size_t fm_layer_elems = (size_t)6144 * D + D * 4096 + 2 * (size_t)h->F * D + D * (size_t)h->F + 2 * D;
+  // the acoustic transformer's layers are sharded like the backbone's (same shapes)
+  const size_t fm_layer_elems = layer_elems;
   size_t elems = layer_elems * h->L + (size_t)h->V * D + (size_t)h->AV * D + D;
   if (c.enable_fm)
     elems += fm_layer_elems * h->FL + D * 36 + (size_t)(h->SEMV + D) * D + D * D + D + 36 * D;
@@ -1105,19 +1092,21 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     for (int l = 0; l < h->FL; ++l) {
       LayerW& W = h->fm_layers[l];
       const std::string pre = p + "layers." + std::to_string(l) + ".";
-      W.wqkv = alloc_h((size_t)6144 * D);
-      W.wo = alloc_h(D * 4096);
-      W.w13 = alloc_h(2 * (size_t)Fm * D);
-      W.w2 = alloc_h(D * (size_t)Fm);
+      W.wqkv = alloc_h((size_t)h->QKVD * D);
+      W.wo = alloc_h(D * (size_t)h->QD);
+      W.w13 = alloc_h(2 * (size_t)h->Fl * D);
+      W.w2 = alloc_h(D * (size_t)h->Fl);
       W.attn_norm = alloc_h(D);
       W.ffn_norm = alloc_h(D);
-      add_tensor(h, pre + "attention.wq.weight", W.wqkv, D, Q, D, Q, D, 0, 0, false);
-      add_tensor(h, pre + "attention.wk.weight", W.wqkv + (size_t)Q * D, D, KV, D, KV, D, 0, 0, false);
-      add_tensor(h, pre + "attention.wv.weight", W.wqkv + (size_t)(Q + KV) * D, D, KV, D, KV, D, 0, 0, false);
-      add_tensor(h, pre + "attention.wo.weight", W.wo, Q, D, Q, D, Q, 0, 0, false);
-      add_tensor(h, pre + "feed_forward.w1.weight", W.w13, D, Fm, D, Fm, D, 0, 0, false);
-      add_tensor(h, pre + "feed_forward.w3.weight", W.w13 + (size_t)Fm * D, D, Fm, D, Fm, D, 0, 0, false);
-      add_tensor(h, pre + "feed_forward.w2.weight", W.w2, Fm, D, Fm, D, Fm, 0, 0, false);
+      const long long r = h->rank;
+      add_tensor(h, pre + "attention.wq.weight", W.wqkv, D, h->QD, D, Q, D, r * h->QD, 0, false);
+      add_tensor(h, pre + "attention.wk.weight", W.wqkv + (size_t)h->QD * D, D, h->KVD, D, KV, D, r * h->KVD, 0, false);
+      add_tensor(h, pre + "attention.wv.weight", W.wqkv + (size_t)(h->QD + h->KVD) * D, D, h->KVD, D, KV, D,
+                 r * h->KVD, 0, false);
+      add_tensor(h, pre + "attention.wo.weight", W.wo, h->QD, D, h->QD, D, Q, 0, r * h->QD, false);
+      add_tensor(h, pre + "feed_forward.w1.weight", W.w13, D, h->Fl, D, Fm, D, r * h->Fl, 0, false);
+      add_tensor(h, pre + "feed_forward.w3.weight", W.w13 + (size_t)h->Fl * D, D, h->Fl, D, Fm, D, r * h->Fl, 0, false);
+      add_tensor(h, pre + "feed_forward.w2.weight", W.w2, h->Fl, D, h->Fl, D, Fm, 0, r * h->Fl, false);
       add_tensor(h, pre + "attention_norm.weight", W.attn_norm, D, 1, D, 1, D, 0, 0, true);
       add_tensor(h, pre + "ffn_norm.weight", W.ffn_norm, D, 1, D, 1, D, 0, 0, true);
     }
@@ -1260,7 +1249,6 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     // need the NCCL communicator of vx_tp_init
     h->use_tb = true;
     if ((rc = setup_tb(h))) { *out = h; return rc; }
-    h->fm_tc = h->tp == 1 && c.enable_fm;   // the acoustic transformer is replicated under TP (per-op GEMVs)
   }
   *out = h;
   return VX_OK;
