@@ -147,6 +147,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   griddep_launch();
+  // The weight tiles do not depend on the previous kernel: the first ring's worth of them
+  // starts streaming before the dependency wait, under the previous kernel's tail.
+  const int pre = min(nk, C::kStages);
+  if (warp == 0 && lane == 0)
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], C::kStage);   // W now, X after the wait: one phase
+      tma_load_2d(smem + i * C::kStage, &wmap, (kc0 + i) * kBK, m0, &full[i]);
+    }
   griddep_wait();   // X (and Y when accumulating) come from the previous kernel
 
   if (warp == 0 && lane == 0) {
@@ -157,8 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ CU
       if (i >= C::kStages && !mbar_wait(&empty[s], (uint32_t)((i / C::kStages) - 1) & 1u, kDevTimeoutEmpty)) break;
       uint8_t* st = smem + s * C::kStage;
       const int kx = (kc0 + i) * kBK;
-      mbar_arrive_expect_tx(&full[s], C::kStage);
-      tma_load_2d(st, &wmap, kx, m0, &full[s]);
+      if (i >= pre) {
+        mbar_arrive_expect_tx(&full[s], C::kStage);
+        tma_load_2d(st, &wmap, kx, m0, &full[s]);
+      }
       tma_load_2d(st + C::kA, &xhi_map, kx, n0, &full[s]);
       tma_load_2d(st + C::kA + C::kB, &xlo_map, kx, n0, &full[s]);
       issued = i + 1;
