@@ -637,7 +637,15 @@ def run_trace(args):
         d = {"span_us": span,
              "consumers_median_us": np.mean([np.median(done[:, k] - rel[:, k]) for k in ks]) / 1e3,
              "consumers_max_us": np.mean([np.max(done[:, k] - rel[:, k]) for k in ks]) / 1e3}
-        if nm != "attention":
+        if nm == "attention":
+            # CTAs holding an attention item: stamps of its K/V pair landing, split partial
+            # stored, merge ticket taken, relative to the phase's release
+            for slot, key in ((4, "kv_pair_in_smem_us"), (5, "partial_stored_us"), (6, "ticket_taken_us")):
+                v = [np.median(tr[tr[:, k, slot] > 0, k, slot] - rel[tr[:, k, slot] > 0, k] - t0) for k in ks
+                     if (tr[:, k, slot] > 0).any()]
+                if v:
+                    d[key] = float(np.mean(v)) / 1e3
+        else:
             d["prologue_us"] = np.mean([np.median(pro[:, k] - rel[:, k]) for k in ks]) / 1e3
             d["epilogue_lag_us"] = np.mean([arr[:, k].max() - done[:, k].max() for k in ks]) / 1e3
             d["stage_wait_us"] = np.mean([np.median(tr[:, k, 4]) for k in ks]) / mhz

@@ -231,9 +231,13 @@ int vx_synchronize(vx_handle* h);
  *                        all-reduce), so that phase starts without a grid barrier; 0: the
  *                        epilogues add into the residual and the next phase waits at a
  *                        grid barrier (tp_size 1 only).
- *   "l2_prefetch_tiles"  0-32 (default 3): weight tiles the persistent kernel prefetches
+ *   "l2_prefetch_tiles"  0-32 (default 2): weight tiles the persistent kernel prefetches
  *                        into L2 ahead of its shared-memory ring.
- *   "wait_limit"         polls before a wait of the persistent kernel on a grid barrier
+ *   "early_kv_pair"      1 (default): the persistent kernel copies each CTA's first pair
+ *                        of K/V pages into shared memory while the QKV phase runs (the
+ *                        current position's row is patched in afterwards); 0: the copy
+ *                        starts after the barrier that ends the QKV phase.
+ *   "wait_limit"        polls before a wait of the persistent kernel on a grid barrier
  *                        or on a tensor-parallel peer's all-reduce words gives up and the
  *                        call returns VX_E_DEVICE (0, default: 2^27 / 2^24 polls, seconds).
  *   "tp_loopback"        1 (test support, tp_size > 1, one process): every peer receive

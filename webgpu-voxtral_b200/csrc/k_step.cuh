@@ -69,7 +69,7 @@ constexpr int kAttnBytes = 65536;                          // a pair of K/V page
 constexpr int kOffBars = kOffAttn + kAttnBytes;            // mbarriers
 constexpr int kOffRed = kOffBars + 256;
 constexpr int kOffScratch = kOffRed + kRedSlots * kCW * kMaxVals * 4;
-constexpr int kScratchBytes = 4096;   // [0,256) combine weights / norm partials, [768,805) codes
+constexpr int kScratchBytes = 4096;   // [0,256) norm partials, [256,768) q of the attention item, [768,805) codes
 constexpr size_t kSmemBytes = (size_t)kOffScratch + kScratchBytes + 1024;   // + alignment slack
 
 // tiles per reduction group (group outputs TG * rows-per-tile <= 32)
@@ -97,6 +97,7 @@ struct StepParams {
   unsigned* bar;          // grid barrier counter, zero at launch
   unsigned long long* trace;  // nullable: [G][kTraceFrames][phases][kTraceSlots] (see trace_mark)
   int prefetch_ahead;     // weight tiles prefetched into L2 ahead of the ring (0..kMaxPrefetchAhead)
+  int early_kv;           // copy each CTA's first K/V pair during the QKV phase (preload_kv)
   int n_frames;
   int mode0, token0;      // embedding of the first step
   int mode_next;          // embedding of later steps
@@ -115,6 +116,9 @@ struct StepParams {
   unsigned long long* peer_recv[kMaxTp];   // every rank's receive words (index = rank; own one included)
   unsigned long long* hx;             // local tagged words of the summed residual [2 parity][D]
   unsigned long long ar_base;         // all-reduces completed before this launch
+  // AR kernels: the QKV epilogues' outputs as tagged words [QD + 2 KVD] (K / V rows
+  // f16-rounded; local memory, zeroed at allocation), read by the attention phase
+  unsigned long long* qkv_t;
 };
 
 struct Smem {
@@ -149,6 +153,10 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 }
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Generic-proxy stores to shared memory ordered before later TMA writes to it.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
   unsigned v;
@@ -244,7 +252,9 @@ __device__ __forceinline__ void grid_arrive_warp(const StepParams& p, int lane, 
 // globaltimer stamps (ns) [0] = consumers released, [1] = consumers done, [2] = epilogue
 // arrival, [3] = consumers' x' prologue done (GEMV phases); SM cycles spent waiting
 // [4] = consumer warp 0 on weight stages, [5] = consumer warp 0 on reduction slots,
-// [6] = epilogue warp on reduction results.
+// [6] = epilogue warp on reduction results.  Attention phase, stamps of the CTA's
+// first item: [4] K/V pair in shared memory, [5] split partial stored, [6] merge
+// ticket taken.
 constexpr int kTraceFrames = 2, kTraceSlots = 8;
 __device__ __forceinline__ void trace_val(const StepParams& p, int c, int f, int kl, int which, int L, int t0,
                                           unsigned long long v) {
@@ -597,8 +607,10 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
           const float x0 = even ? val : other, x1 = even ? other : val;
           out = even ? __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
         }
+        const uint32_t tag = (uint32_t)(ar_k + 1);
         if (row < TD::QD) {
-          p.q[row] = out;
+          if (p.qkv_t) st_tagged(p.qkv_t + row, out, tag);
+          else p.q[row] = out;
         } else {
           const int kvr = row - TD::QD;
           const int kv = kvr >= TD::KVD ? 1 : 0;
@@ -609,7 +621,9 @@ __device__ __forceinline__ bool epilogue(const StepParams& p, Smem& s, uint32_t&
           } else {
             const int page = p.kv.page_table[(long long)p.slot * p.kv.max_pages + lp];
             const long long prow = gemv::kv_row(p.kv, page, layer, kv, rr >> 7, pos % p.kv.page_size);
-            p.kv.pool[prow * HD + (rr & 127)] = __float2half_rn(out);
+            const __half hv = __float2half_rn(out);
+            p.kv.pool[prow * HD + (rr & 127)] = hv;
+            if (p.qkv_t) st_tagged(p.qkv_t + row, __half2float(hv), tag);
           }
         }
       }
@@ -651,42 +665,73 @@ __device__ __forceinline__ void issue_pair(const StepParams& p, const CUtensorMa
     tma_load_2d(dst + 24576, kvmap, 64, vrow, s.afull);
   }
 }
-// Called at the start of the QKV phase: L2 prefetch of the K/V pages of this CTA's
-// attention items, so that the attention phase's TMA loads hit L2.  The current
-// position's row is written later in the QKV phase; L2 stays coherent with that write.
+// Called by the consumers at the start of the QKV phase.  With p.early_kv, thread 0
+// copies the first K/V pair of this CTA's first attention item into the attention
+// buffer, so that the copy runs under the QKV phase instead of after the barrier that
+// ends it; the row of `pos` in that pair is stale (this phase writes it) and the
+// attention phase patches it in shared memory from the KV pool.  The other pages of
+// this CTA's items are prefetched into L2, so that their TMA loads hit L2.  Returns
+// whether the first pair was issued early (the same value on every thread).
 template <int N>
-__device__ __forceinline__ void prefetch_kv(const StepParams& p, int layer, int pos, int c, int G, int ctid) {
-  if (ctid != 0) return;
+__device__ __forceinline__ bool preload_kv(const StepParams& p, const CUtensorMap* kvmap, Smem& s, int layer, int pos,
+                                           int c, int G, int ctid, uint32_t ait, bool& a_pending, uint32_t& a_par) {
   int npages, pps, n_used;
   split_plan(p, pos, npages, pps, n_used);
+  const bool pre = p.early_kv && c < Tp<N>::NKV * p.n_splits && c % p.n_splits < n_used;
+  if (ctid != 0) return pre;
   const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
   for (int item = c; item < Tp<N>::NKV * p.n_splits; item += G) {
     const int kvh = item / p.n_splits, split = item % p.n_splits;
     if (split >= n_used) continue;
     const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
-    for (int pg = pg0; pg < pg1; ++pg) {
+    int pg = pg0;
+    if (item == c && pre) {
+      const int npair = min(2, pg1 - pg0);
+      if (!error_set()) {
+        a_pending = true;
+        a_par = ait & 1u;
+        issue_pair(p, kvmap, s, layer, kvh, pg0, npair);
+      }
+      pg += npair;
+    }
+    for (; pg < pg1; ++pg) {
       const int phys = ptab[pg];
       prefetch_l2(p.kv.pool + gemv::kv_row(p.kv, phys, layer, 0, kvh, 0) * HD, 64u * HD * 2u);
       prefetch_l2(p.kv.pool + gemv::kv_row(p.kv, phys, layer, 1, kvh, 0) * HD, 64u * HD * 2u);
     }
   }
+  return pre;
+}
+
+// Value pair of two consecutive tagged words, once both carry `tag` (bounded poll).
+__device__ __forceinline__ float2 tagged_pair(ulonglong2 w, const unsigned long long* p, uint32_t tag, uint32_t limit) {
+  const float x = (uint32_t)(w.x >> 32) == tag ? __uint_as_float((uint32_t)w.x) : wait_tagged(p, tag, limit);
+  const float y = (uint32_t)(w.y >> 32) == tag ? __uint_as_float((uint32_t)w.y) : wait_tagged(p + 1, tag, limit);
+  return make_float2(x, y);
 }
 
 // Control flow is uniform across the 256 consumer threads (every named barrier is
 // reached by all of them); after a device error the work is skipped, not the barriers.
-template <int N>
+// TQ (the AR kernels): no grid barrier before this phase; q and the current position's
+// K / V rows arrive as tagged words from the QKV epilogues (p.qkv_t, tag `tag`), so an
+// item starts as soon as the words of its KV head have landed.  !TQ: q from p.q after
+// the QKV barrier.  Either way the splits' partials go to p.part, the last split to
+// take a ticket merges them into p.att, and the phase ends at a grid barrier.
+template <int N, bool TQ>
 __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap* kvmap, Smem& s, uint32_t& ait,
-                                          bool& a_pending, int layer, int pos, int c, int G, int cw,
-                                          int lane, int ctid) {
+                                          bool& a_pending, uint32_t& a_par, bool pre, int layer, int pos, int c,
+                                          int G, int cw, int lane, int ctid, int f, int kl, uint32_t tag) {
+  using TD = Tp<N>;
   const int seq = pos + 1;
   int npages, pps, n_used;
   split_plan(p, pos, npages, pps, n_used);
   const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
+  const uint32_t limit = p.wait_limit ? p.wait_limit : kTagPolls;
   const float scale = 0.08838834764831845f;   // 1/sqrt(128) rounded to f32
   const int g = lane >> 2, hq = g & 3;
   const bool lo_part = g >= 4;
   const int half_pair = cw >> 2, grp = cw & 3;
-  for (int item = c; item < Tp<N>::NKV * p.n_splits; item += G) {
+  for (int item = c; item < TD::NKV * p.n_splits; item += G) {
     const int kvh = item / p.n_splits, split = item % p.n_splits;
     if (split >= n_used) continue;   // uniform: no positions in this split
     const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
@@ -698,29 +743,89 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
     for (int pp = pg0; pp < pg1; pp += 2) {
       const int npair = min(2, pg1 - pp);
       const bool go = !error_set();
-      if (ctid == 0 && go) {
+      const bool early = pre && item == c && pp == pg0;   // issued by preload_kv
+      if (ctid == 0 && go && !early) {
         a_pending = true;
+        a_par = ait & 1u;
         issue_pair(p, kvmap, s, layer, kvh, pp, npair);
       }
-      if (pp == pg0) {
-      // q fragments (hi rows 0-3, lo rows 4-7) for the 4 heads of this KV head, loaded
-      // while the first K/V pair is in flight
-      const float* qh = p.q + (long long)(kvh * GQA + hq) * HD;
-  #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int cc = kk * 16 + (lane & 3) * 2;
-        float v0 = qh[cc], v1 = qh[cc + 1], v8 = qh[cc + 8], v9 = qh[cc + 9];
-        if (lo_part) {
-          v0 -= __half2float(__float2half_rn(v0)); v1 -= __half2float(__float2half_rn(v1));
-          v8 -= __half2float(__float2half_rn(v8)); v9 -= __half2float(__float2half_rn(v9));
-        }
-        qa0[kk] = pack_half2(v0, v1);
-        qa2[kk] = pack_half2(v8, v9);
+      // The pair holding position pos may hold a stale copy of its row: copied before
+      // the QKV phase wrote it (early pair; TAG: any pair, as no barrier precedes this
+      // phase).  The row is stored over it after the copy lands: TAG from the tagged
+      // words (f16-rounded values), else from the KV pool.
+      const int lp = pos >> 6;
+      const bool patch = (TQ || early) && lp >= pp && lp < pp + npair;
+      uint4 nrow = make_uint4(0u, 0u, 0u, 0u);
+      ulonglong2 trow = make_ulonglong2(0ull, 0ull);
+      const unsigned long long* trow_p =
+          TQ ? p.qkv_t + TD::QD + (ctid >> 6) * TD::KVD + kvh * HD + (ctid & 63) * 2 : nullptr;
+      if constexpr (TQ) {
+        if (patch && go && ctid < 128) trow = ld_tagged2(trow_p);
+      } else {
+        if (patch && go && ctid < 32)
+          nrow = __ldcg(reinterpret_cast<const uint4*>(
+                            p.kv.pool + gemv::kv_row(p.kv, ptab[lp], layer, ctid >> 4, kvh, pos & 63) * HD) +
+                        (ctid & 15));
       }
+      if (pp == pg0) {
+        // q fragments (hi rows 0-3, lo rows 4-7) for the 4 heads of this KV head, loaded
+        // while the first K/V pair is in flight
+        float qv[8][4];
+        if constexpr (TQ) {
+          // the 512 words of q of this KV head: two per thread, staged in shared memory
+          float* qs = s.scratch + 256;
+          const unsigned long long* qt = p.qkv_t + (long long)kvh * GQA * HD + ctid * 2;
+          const float2 v = go ? tagged_pair(ld_tagged2(qt), qt, tag, limit) : make_float2(0.f, 0.f);
+          qs[ctid * 2] = v.x;
+          qs[ctid * 2 + 1] = v.y;
+          named_bar_sync(1, kCW * 32);
+          const float* qh = qs + hq * HD;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int cc = kk * 16 + (lane & 3) * 2;
+            qv[kk][0] = qh[cc]; qv[kk][1] = qh[cc + 1]; qv[kk][2] = qh[cc + 8]; qv[kk][3] = qh[cc + 9];
+          }
+        } else {
+          const float* qh = p.q + (long long)(kvh * GQA + hq) * HD;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int cc = kk * 16 + (lane & 3) * 2;
+            qv[kk][0] = qh[cc]; qv[kk][1] = qh[cc + 1]; qv[kk][2] = qh[cc + 8]; qv[kk][3] = qh[cc + 9];
+          }
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          float v0 = qv[kk][0], v1 = qv[kk][1], v8 = qv[kk][2], v9 = qv[kk][3];
+          if (lo_part) {
+            v0 -= __half2float(__float2half_rn(v0)); v1 -= __half2float(__float2half_rn(v1));
+            v8 -= __half2float(__float2half_rn(v8)); v9 -= __half2float(__float2half_rn(v9));
+          }
+          qa0[kk] = pack_half2(v0, v1);
+          qa2[kk] = pack_half2(v8, v9);
+        }
       }
       const bool w_ok = go && mbar_wait(s.afull, ait & 1u, kDevTimeoutFull);
       if (w_ok && ctid == 0) a_pending = false;
       ++ait;
+      if (item == c && pp == pg0) trace_mark(p, c, f, kl, 4, p.n_layers, ctid);
+      if (patch) {
+        if constexpr (TQ) {
+          if (w_ok && ctid < 128) {
+            const float2 v = tagged_pair(trow, trow_p, tag, limit);
+            const int col = (ctid & 63) * 2;
+            *reinterpret_cast<__half2*>(s.attn + (lp - pp) * 32768 + (ctid >> 6) * 16384 + attn::swz(pos & 63, col) +
+                                        (col & 7) * 2) = __floats2half2_rn(v.x, v.y);
+            fence_proxy_async_shared();   // the next TMA into this buffer is ordered after the store
+          }
+        } else {
+          if (w_ok && ctid < 32) {
+            *reinterpret_cast<uint4*>(s.attn + (lp - pp) * 32768 + (ctid >> 4) * 16384 +
+                                      attn::swz(pos & 63, (ctid & 15) * 8)) = nrow;
+            fence_proxy_async_shared();
+          }
+        }
+        named_bar_sync(1, kCW * 32);
+      }
       if (w_ok && half_pair < npair) {
         const int pg = pp + half_pair;
         const uint32_t kbase = smem_u32(s.attn + half_pair * 32768);
@@ -792,6 +897,7 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
         w[2 + d] = o[j][0];
         w[3 + d] = o[j][1];
       }
+      fence_proxy_async_shared();   // scratch in the pair buffer, which TMA overwrites next
     }
     named_bar_sync(1, kCW * 32);
     float* part = p.part + ((long long)kvh * p.n_splits + split) * (GQA * PS);
@@ -805,20 +911,22 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
 #pragma unroll
         for (int w = 0; w < kCW; ++w) {
           const float* ww = ws + (w * GQA + h) * attn::kPartStride;
-          const float f = ww[0] == -INFINITY ? 0.f : expf(ww[0] - M);
-          L += ww[1] * f;
-          O += ww[2 + d] * f;
+          const float fw = ww[0] == -INFINITY ? 0.f : expf(ww[0] - M);
+          L += ww[1] * fw;
+          O += ww[2 + d] * fw;
         }
       }
       part[h * PS + 4 + d] = O;
       if (d == 0) { part[h * PS] = M; part[h * PS + 1] = L; }
     }
     named_bar_sync(1, kCW * 32);
+    if (item == c) trace_mark(p, c, f, kl, 5, p.n_layers, ctid);
     // The last split of this KV head to finish merges all n_used splits into att.
     // Each thread owns 2 output dims of one head and issues all its loads at once.
     int* s_flag = reinterpret_cast<int*>(s.scratch + 1020);
     if (ctid == 0) *s_flag = (atom_add_acq_rel(&p.tickets[kvh], 1) == n_used - 1);
     named_bar_sync(1, kCW * 32);
+    if (item == c) trace_mark(p, c, f, kl, 6, p.n_layers, ctid);
     if (*s_flag) {
       const int h = ctid >> 6, d0 = (ctid & 63) * 2;
       const float* base = p.part + ((long long)kvh * p.n_splits * GQA + h) * PS;
@@ -969,7 +1077,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
         const int o3 = (int)((tiles_before + TD::TQKV + TD::TO + TD::TW13) % G);
         const int kl = 1 + 5 * l;
         const unsigned long long k_o = kf + 2 * l, k_w2 = kf + 2 * l + 1;
-        if (!epilogue<6, gemv::kQkv, kTgQKV, kCW, N>(p, s, rit, nullptr, TD::QKVD, TD::TQKV, o0, c, G, lane, l, pos, f, kl))
+        if (!epilogue<6, gemv::kQkv, kTgQKV, kCW, N>(p, s, rit, nullptr, TD::QKVD, TD::TQKV, o0, c, G, lane, l, pos, f, kl,
+                                                     k_o))
           return;
         trace_mark(p, c, f, kl, 2, L, lane);
         if constexpr (!AR) {
@@ -1002,7 +1111,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
   const int per = (D + G - 1) / G;        // embedding / norm slice of this CTA
   const int e0 = c * per, e1 = min(D, e0 + per);
   uint32_t* codes = reinterpret_cast<uint32_t*>(s.scratch + 768);
-  bool a_pending = false;   // an attention TMA pair is in flight (thread 0)
+  bool a_pending = false;   // an attention TMA pair is in flight (thread 0) ...
+  uint32_t a_par = 0;       // ... and the parity of its completion on s.afull
   // tensor parallelism: the residual alternates between p.h and p.h2 per all-reduce
   // (all-reduce k reads h[k & 1] and its parity k & 1 of the receive buffer, writes
   // h[(k + 1) & 1]); every launch starts at an even all-reduce index, so EMBED
@@ -1071,7 +1181,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       const bool ar_qkv = AR && l > 0;
       grid_wait<N>(p, phase * G, ctid, ar_qkv);
       trace_mark(p, c, f, kl, 0, L, ctid);
-      prefetch_kv<N>(p, l, pos, c, G, ctid);
+      const bool kv_pre = preload_kv<N>(p, &kvmap, s, l, pos, c, G, ctid, ait, a_pending, a_par);
       {
         const ArIn a = ar_qkv ? ar_in(k_prev) : ArIn{};
         consume<6, 3, true, kTgQKV, kCW, N>(p, s, it, rit, hb[0], W.attn_norm, D, TD::TQKV, o0, c, G, cw, lane, pos, f,
@@ -1079,10 +1189,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
       }
       trace_mark(p, c, f, kl, 1, L, ctid);
       ++phase;
-      // ---- attention
-      grid_wait<N>(p, phase * G, ctid);
+      // ---- attention (AR: its inputs arrive as tagged words, no grid barrier before it)
+      if constexpr (!AR) grid_wait<N>(p, phase * G, ctid);
       trace_mark(p, c, f, kl + 1, 0, L, ctid);
-      attention<N>(p, &kvmap, s, ait, a_pending, l, pos, c, G, cw, lane, ctid);
+      attention<N, AR>(p, &kvmap, s, ait, a_pending, a_par, kv_pre, l, pos, c, G, cw, lane, ctid, f, kl + 1,
+                       (uint32_t)(k_o + 1));
       trace_mark(p, c, f, kl + 1, 1, L, ctid);
       if (ctid == 0) red_release_add(p.bar, 1u);
       ++phase;
@@ -1143,6 +1254,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
             *reinterpret_cast<float4*>(hs + cols[u]) = v[u];
             if (c == 0) *reinterpret_cast<float4*>(fa.h_new + cols[u]) = v[u];
           }
+          fence_proxy_async_shared();   // hs lies in the attention buffer, which TMA overwrites next
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) ss += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
@@ -1174,7 +1286,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_steps(const __grid_const
     }
   }
   // an attention copy left in flight by an error must land before the CTA exits
-  if (ctid == 0 && a_pending) mbar_wait_drain(s.afull, (ait - 1) & 1u);
+  if (ctid == 0 && a_pending) mbar_wait_drain(s.afull, a_par);
   // slot bookkeeping once every CTA has finished the last step
   if (c == 0) {
     grid_wait<N>(p, phase * G, ctid);

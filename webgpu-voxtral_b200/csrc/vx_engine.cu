@@ -157,6 +157,8 @@ struct vx_handle {
   bool p2p_ready = false;
   float* h2 = nullptr;
   unsigned long long ar_base = 0;
+  // persistent kernel (AR form): q / K / V rows handed to its attention phase as tagged words
+  unsigned long long* mk_tags = nullptr;
   bool coop = false;
 
   // persistent decode kernel (k_step.cuh): layer table and grid-barrier counter
@@ -164,7 +166,8 @@ struct vx_handle {
   mk::LayerPtrs* d_layers = nullptr;
   unsigned* d_bar = nullptr;
   unsigned long long* d_trace = nullptr;   // phase trace of the next persistent launch (vx_trace)
-  int prefetch_ahead = 3;   // persistent kernel: L2 lookahead in weight tiles (option l2_prefetch_tiles; measured best)
+  int prefetch_ahead = 2;   // persistent kernel: L2 lookahead in weight tiles (option l2_prefetch_tiles; measured best)
+  bool early_kv = true;     // persistent kernel: first K/V pair copied during the QKV phase (option early_kv_pair)
   uint32_t wait_limit = 0;  // persistent kernel: polls before a barrier / peer wait gives up (option wait_limit; 0 = built-in)
   bool tp_loopback = false; // option tp_loopback: every peer receive buffer is this handle's own (test support)
   bool tagged = true;       // tp 1: residual handed over as tagged words (option residual_handoff)
@@ -293,6 +296,7 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
   sp.slots = h->slots; sp.slot = slot; sp.bar = h->d_bar;
   sp.trace = h->trace_armed ? h->d_trace : nullptr;
   sp.prefetch_ahead = h->prefetch_ahead;
+  sp.early_kv = h->early_kv ? 1 : 0;
   sp.dbg = dbg; sp.dbg_frame = dbg_frame;
   sp.wait_limit = h->wait_limit;
   h->trace_armed = false;
@@ -318,6 +322,7 @@ int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, in
     for (int r = 0; r < h->tp; ++r) sp.peer_recv[r] = reinterpret_cast<unsigned long long*>(h->p2p_peer[r]);
     sp.hx = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(h->p2p_buf) + kP2pHxOff);
     sp.ar_base = h->ar_base;
+    sp.qkv_t = h->mk_tags;
   }
   h->launches++;
   switch (h->tp) {
@@ -1235,6 +1240,13 @@ int vx_create(const vx_config* cfg, vx_handle** out) {
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->dev);
     h->coop = coop != 0;
     h->use_mk = h->coop && h->tp == 1;   // TP: enabled by vx_tp_p2p_open
+    if (h->coop) {
+      // the QKV epilogues' outputs as tagged words for the attention phase (tag 0 never matches)
+      const size_t words = (size_t)h->QKVD;
+      if (cudaMalloc((void**)&h->mk_tags, words * 8) != cudaSuccess || cudaMemset(h->mk_tags, 0, words * 8) != cudaSuccess) {
+        *out = h; return h->fail(VX_E_NOMEM, "tagged q / K / V words");
+      }
+    }
     if (h->coop && h->tp == 1) {
       // the persistent kernel's tagged residual words (a one-rank all-reduce)
       if (cudaMalloc(&h->p2p_buf, kP2pBytes) != cudaSuccess || cudaMemset(h->p2p_buf, 0, kP2pBytes) != cudaSuccess) {
@@ -1268,6 +1280,7 @@ void vx_destroy(vx_handle* h) {
   for (int r = 0; r < mk::kMaxTp; ++r)
     if (h->p2p_peer[r] && h->p2p_peer[r] != h->p2p_buf) cudaIpcCloseMemHandle(h->p2p_peer[r]);
   if (h->p2p_buf) cudaFree(h->p2p_buf);
+  if (h->mk_tags) cudaFree(h->mk_tags);
   if (h->arena) cudaFree(h->arena);
   if (h->d_layers) cudaFree(h->d_layers);
   if (h->d_trace) cudaFree(h->d_trace);
@@ -2004,6 +2017,9 @@ int vx_set_option(vx_handle* h, const char* name, int64_t value) {
     if (value < 0 || value > mk::kMaxPrefetchAhead)
       return h->fail(VX_E_RANGE, "l2_prefetch_tiles must lie in [0, %d]", mk::kMaxPrefetchAhead);
     h->prefetch_ahead = (int)value;
+  } else if (n == "early_kv_pair") {
+    if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "early_kv_pair must be 0 or 1");
+    h->early_kv = value != 0;
   } else if (n == "wait_limit") {
     if (value < 0 || value > 0xffffffffll) return h->fail(VX_E_RANGE, "wait_limit must lie in [0, 2^32)");
     h->wait_limit = (uint32_t)value;
