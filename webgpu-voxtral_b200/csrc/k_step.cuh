@@ -728,18 +728,19 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
   const int32_t* ptab = p.kv.page_table + (long long)p.slot * p.kv.max_pages;
   const uint32_t limit = p.wait_limit ? p.wait_limit : kTagPolls;
   const float scale = 0.08838834764831845f;   // 1/sqrt(128) rounded to f32
-  const int g = lane >> 2, hq = g & 3;
-  const bool lo_part = g >= 4;
+  // mma operands: query columns n = 2 head + (0: f16 part, 1: f16 remainder), 8 per KV
+  // head; this lane supplies query column lane / 4 and holds head lane % 4's results
+  const int qn = lane >> 2, hd = lane & 3;
   const int half_pair = cw >> 2, grp = cw & 3;
   for (int item = c; item < TD::NKV * p.n_splits; item += G) {
     const int kvh = item / p.n_splits, split = item % p.n_splits;
     if (split >= n_used) continue;   // uniform: no positions in this split
     const int pg0 = split * pps, pg1 = min(npages, pg0 + pps);
     float m_run = -INFINITY, l_run = 0.f;
-    float o[16][4];
-    uint32_t qa0[8], qa2[8];
+    float ot[8][4];   // O^T: 8 tiles of 16 dims x 8 query columns
+    uint32_t qb0[8], qb1[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    for (int i = 0; i < 8; ++i) ot[i][0] = ot[i][1] = ot[i][2] = ot[i][3] = 0.f;
     for (int pp = pg0; pp < pg1; pp += 2) {
       const int npair = min(2, pg1 - pp);
       const bool go = !error_set();
@@ -768,8 +769,8 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
                         (ctid & 15));
       }
       if (pp == pg0) {
-        // q fragments (hi rows 0-3, lo rows 4-7) for the 4 heads of this KV head, loaded
-        // while the first K/V pair is in flight
+        // Q^T fragments (the B operand of S^T = K Q^T) for the 4 heads of this KV head,
+        // loaded while the first K/V pair is in flight
         float qv[8][4];
         if constexpr (TQ) {
           // the 512 words of q of this KV head: two per thread, staged in shared memory
@@ -779,14 +780,14 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
           qs[ctid * 2] = v.x;
           qs[ctid * 2 + 1] = v.y;
           named_bar_sync(1, kCW * 32);
-          const float* qh = qs + hq * HD;
+          const float* qh = qs + (qn >> 1) * HD;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const int cc = kk * 16 + (lane & 3) * 2;
             qv[kk][0] = qh[cc]; qv[kk][1] = qh[cc + 1]; qv[kk][2] = qh[cc + 8]; qv[kk][3] = qh[cc + 9];
           }
         } else {
-          const float* qh = p.q + (long long)(kvh * GQA + hq) * HD;
+          const float* qh = p.q + (long long)(kvh * GQA + (qn >> 1)) * HD;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const int cc = kk * 16 + (lane & 3) * 2;
@@ -796,12 +797,12 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           float v0 = qv[kk][0], v1 = qv[kk][1], v8 = qv[kk][2], v9 = qv[kk][3];
-          if (lo_part) {
+          if (qn & 1) {
             v0 -= __half2float(__float2half_rn(v0)); v1 -= __half2float(__float2half_rn(v1));
             v8 -= __half2float(__float2half_rn(v8)); v9 -= __half2float(__float2half_rn(v9));
           }
-          qa0[kk] = pack_half2(v0, v1);
-          qa2[kk] = pack_half2(v8, v9);
+          qb0[kk] = pack_half2(v0, v1);
+          qb1[kk] = pack_half2(v8, v9);
         }
       }
       const bool w_ok = go && mbar_wait(s.afull, ait & 1u, kDevTimeoutFull);
@@ -830,72 +831,58 @@ __device__ __forceinline__ void attention(const StepParams& p, const CUtensorMap
         const int pg = pp + half_pair;
         const uint32_t kbase = smem_u32(s.attn + half_pair * 32768);
         const uint32_t vbase = kbase + 16384;
-        float sacc[2][4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
         const int mat = lane >> 3, r8 = lane & 7;
+        // S^T = K Q^T over the warp's 16 positions (rows) and the 8 query columns
+        float st[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(b0, b1, b2, b3, kbase + attn::swz(grp * 16 + (mat >> 1) * 8 + r8, kk * 16 + (mat & 1) * 8));
-          mma_16816(sacc[0], qa0[kk], 0u, qa2[kk], 0u, b0, b1);
-          mma_16816(sacc[1], qa0[kk], 0u, qa2[kk], 0u, b2, b3);
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(a0, a1, a2, a3, kbase + attn::swz(grp * 16 + (mat & 1) * 8 + r8, kk * 16 + (mat >> 1) * 8));
+          mma_16816(st, a0, a1, a2, a3, qb0[kk], qb1[kk]);
         }
-        float sc[2][2], mloc = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float fd = sacc[j][e] + __shfl_xor_sync(0xffffffffu, sacc[j][e], 16);
-            const int ppos = pg * 64 + grp * 16 + j * 8 + (lane & 3) * 2 + e;
-            sc[j][e] = ppos < seq ? fd * scale : -INFINITY;
-            mloc = fmaxf(mloc, sc[j][e]);
-          }
-        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+        // head hd at positions p0 and p0 + 8: the two query columns of the head summed
+        const int p0 = pg * 64 + grp * 16 + qn;
+        const float s0 = p0 < seq ? (st[0] + st[1]) * scale : -INFINITY;
+        const float s1 = p0 + 8 < seq ? (st[2] + st[3]) * scale : -INFINITY;
+        float mloc = fmaxf(s0, s1);
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 4));
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 8));
+        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 16));
         const float m_new = fmaxf(m_run, mloc);
         const float corr = (m_new == -INFINITY) ? 1.f : expf(m_run - m_new);
-        float psum = 0.f, pv[2][2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float pe = sc[j][e] == -INFINITY ? 0.f : expf(sc[j][e] - m_new);
-            psum += pe;
-            pv[j][e] = lo_part ? pe - __half2float(__float2half_rn(pe)) : pe;
-          }
-        const uint32_t pa0 = pack_half2(pv[0][0], pv[0][1]), pa2 = pack_half2(pv[1][0], pv[1][1]);
-        l_run = l_run * corr + psum;
+        const float e0 = s0 == -INFINITY ? 0.f : expf(s0 - m_new);
+        const float e1 = s1 == -INFINITY ? 0.f : expf(s1 - m_new);
+        l_run = l_run * corr + (e0 + e1);
         m_run = m_new;
+        // P^T (the B operand of O^T += V^T P^T): (f16 part, remainder) pairs in S^T's
+        // layout, each 8x8 tile transposed in registers
+        const uint32_t pb0 = movmatrix_trans(pack_half2(e0, e0 - __half2float(__float2half_rn(e0))));
+        const uint32_t pb1 = movmatrix_trans(pack_half2(e1, e1 - __half2float(__float2half_rn(e1))));
 #pragma unroll
-        for (int j = 0; j < 16; ++j) { o[j][0] *= corr; o[j][1] *= corr; }
+        for (int i = 0; i < 8; ++i) {
+          ot[i][0] *= corr; ot[i][1] *= corr; ot[i][2] *= corr; ot[i][3] *= corr;
+        }
 #pragma unroll
-        for (int dt2 = 0; dt2 < 8; ++dt2) {
-          uint32_t v0, v1, v2, v3;
-          ldmatrix_x4_trans(v0, v1, v2, v3, vbase + attn::swz(grp * 16 + (mat & 1) * 8 + r8, dt2 * 16 + (mat >> 1) * 8));
-          mma_16816(o[2 * dt2], pa0, 0u, pa2, 0u, v0, v1);
-          mma_16816(o[2 * dt2 + 1], pa0, 0u, pa2, 0u, v2, v3);
+        for (int i = 0; i < 8; ++i) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(a0, a1, a2, a3, vbase + attn::swz(grp * 16 + (mat >> 1) * 8 + r8, i * 16 + (mat & 1) * 8));
+          mma_16816(ot[i], a0, a1, a2, a3, pb0, pb1);
         }
       }
       named_bar_sync(1, kCW * 32);   // the pair buffer is free again
     }
-    // merge the 8 warps (reuse the pair buffer as scratch)
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] += __shfl_xor_sync(0xffffffffu, o[j][0], 16);
-      o[j][1] += __shfl_xor_sync(0xffffffffu, o[j][1], 16);
-    }
+    // merge the 8 warps (reuse the pair buffer as scratch): l over the head's 8 lanes
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 4);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
     float* ws = reinterpret_cast<float*>(s.attn);     // [8 warps][4 heads][130]
-    if (lane < 16) {
-      float* w = ws + (cw * GQA + hq) * attn::kPartStride;
-      if ((lane & 3) == 0) { w[0] = m_run; w[1] = l_run; }
+    {
+      float* w = ws + (cw * GQA + hd) * attn::kPartStride;
+      if (lane < 4) { w[0] = m_run; w[1] = l_run; }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int d = j * 8 + (lane & 3) * 2;
-        w[2 + d] = o[j][0];
-        w[3 + d] = o[j][1];
+      for (int i = 0; i < 8; ++i) {   // f16 part + remainder columns of head hd
+        w[2 + i * 16 + qn] = ot[i][0] + ot[i][1];
+        w[2 + i * 16 + qn + 8] = ot[i][2] + ot[i][3];
       }
       fence_proxy_async_shared();   // scratch in the pair buffer, which TMA overwrites next
     }

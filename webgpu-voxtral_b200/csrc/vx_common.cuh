@@ -159,6 +159,13 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// Transpose of an 8x8 f16 tile held in the mma fragment layout (lane holds row lane/4,
+// columns 2(lane%4), 2(lane%4)+1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
 
 // ---------------------------------------------------------------- math
 // silu(g)*u exactly as the reference writes it: g / (1 + exp(-g)) * u.
