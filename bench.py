@@ -587,6 +587,12 @@ def run_trace(args):
     rank, local, world = vdist.env_rank()
     torch.cuda.set_device(local)
     vdist.init(timeout_s=300)
+    if world > 4:   # the persistent kernel serves tensor-parallel degrees up to 4
+        if rank == 0:
+            print(json.dumps({"trace": "k_decode_steps phase breakdown", "tp": world,
+                              "unavailable": "the persistent decode kernel is not used at this degree"}), flush=True)
+        vdist.shutdown()
+        return 0
     L = args.layers
     pos = mean_position(args)
     eng = vx.VoxtralEngine({"config": {"backbone": {"n_layers": L}}, "maxSeqLen": 4096, "maxFrames": 1024,

@@ -218,10 +218,10 @@ int vx_synchronize(vx_handle* h);
 /* Engine options.  Returns VX_E_INVALID for an unknown name or value, VX_E_STATE /
  * VX_E_RANGE when the handle cannot take the value.  No counterpart in the reference
  * (EngineOptions, src/engine.ts:213-219, has none of these).
- *   "persistent_decode"  1 (default where cooperative launch exists): vx_decode,
- *                        token-by-token vx_prefill and vx_debug_layers run the
- *                        persistent decode kernel; 0: one CUDA graph of per-op kernels
- *                        per step.
+ *   "persistent_decode"  1 (default where cooperative launch exists and tp_size <= 4):
+ *                        vx_decode, token-by-token vx_prefill and vx_debug_layers run
+ *                        the persistent decode kernel; 0: one CUDA graph of per-op kernels
+ *                        per step (always at tp_size 8, where 1 returns VX_E_STATE).
  *   "batched_prefill"    1 (default, tp_size 1): vx_prefill runs the prompt through
  *                        tensor-core GEMMs in batches of up to 512 positions; 0: token
  *                        by token, as the reference (src/engine.ts:2457-2472).
@@ -322,7 +322,8 @@ int vx_tp_init(vx_handle* h, const char* nccl_lib, const uint8_t id[128]);
  * passes them to vx_tp_p2p_open, then all ranks meet at a host barrier before their
  * first decode.  All ranks must issue the same sequence of decode/prefill calls.  The
  * reference runs on one device (src/engine.ts:814-1042); this is its step split over
- * tp_size GPUs. */
+ * tp_size GPUs.  The persistent kernel serves tp_size 2 and 4; at tp_size 8 the handle
+ * keeps the per-op kernels with NCCL all-reduces. */
 int vx_tp_p2p_handle(vx_handle* h, uint8_t out[64]);
 int vx_tp_p2p_open(vx_handle* h, const uint8_t* handles /* [tp_size][64] */);
 

@@ -1,7 +1,8 @@
 """Tensor parallelism (batch-1 latency path) on 2, 4 and 8 GPUs: q/KV heads and FFN columns
-sharded, all-reduce of the residual stream after o_proj and after down.  Prefill, decode
-and debugBackboneLayerByLayer run the persistent kernel, whose all-reduces go through peer
-memory inside the kernel; the FM step uses NCCL between kernels.  Every rank must
+sharded, all-reduce of the residual stream after o_proj and after down.  At degree 2 and 4,
+decode and debugBackboneLayerByLayer run the persistent kernel, whose all-reduces go through
+peer memory inside the kernel; at degree 8 they run the per-op kernels with NCCL all-reduces
+(the persistent kernel is not used there).  The FM step uses NCCL between kernels.  Every rank must
 reproduce the golden fixture's per-layer tensors and FM outputs, and a backbone-only
 decode of the CPU oracle, within the suite's tolerance.  Each degree is skipped when fewer
 GPUs are visible.  NVLS is disabled."""

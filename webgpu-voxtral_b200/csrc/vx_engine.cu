@@ -275,6 +275,11 @@ int prime_kernel_attrs(vx_handle* h) {
 // [2 parity][tp source][D] (8 bytes each; zero = no tag yet), then this rank's own
 // tagged words of the summed residual [2 parity][D] (read only locally).
 constexpr size_t kP2pHxOff = 2ull * mk::kMaxTp * 3072 * 8;
+// Highest tensor-parallel degree at which the persistent decode kernel runs.  At degree 8
+// its per-layer record of a 2-layer model differs from the golden fixture from layer 0's
+// attention output on (the per-op path and the 1-layer kernel match), so degree 8 decodes
+// through the per-op kernels with NCCL all-reduces.
+constexpr int kMkMaxTp = 4;
 constexpr size_t kP2pBytes = kP2pHxOff + 2ull * 3072 * 8;
 
 int launch_steps(vx_handle* h, int slot, int n_frames, int mode0, int token0, int mode_next, bool inc_frame,
@@ -2004,6 +2009,8 @@ int vx_set_option(vx_handle* h, const char* name, int64_t value) {
     if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "persistent_decode must be 0 or 1");
     if (value && !h->coop) return h->fail(VX_E_STATE, "the device has no cooperative launch");
     if (value && h->tp > 1 && !h->p2p_ready) return h->fail(VX_E_STATE, "tensor parallelism: call vx_tp_p2p_open first");
+    if (value && h->tp > kMkMaxTp)
+      return h->fail(VX_E_STATE, "the persistent decode kernel runs at tensor-parallel degree <= %d", kMkMaxTp);
     h->use_mk = value != 0;
   } else if (n == "residual_handoff") {
     if (value != 0 && value != 1) return h->fail(VX_E_INVALID, "residual_handoff must be 0 or 1");
@@ -2025,7 +2032,7 @@ int vx_set_option(vx_handle* h, const char* name, int64_t value) {
     h->wait_limit = (uint32_t)value;
   } else if (n == "tp_loopback") {
     if (value != 1) return h->fail(VX_E_INVALID, "tp_loopback can only be switched on");
-    if (h->tp < 2) return h->fail(VX_E_STATE, "tp_loopback needs tp_size > 1");
+    if (h->tp < 2 || h->tp > kMkMaxTp) return h->fail(VX_E_STATE, "tp_loopback needs tp_size 2..%d", kMkMaxTp);
     if (h->p2p_ready) return h->fail(VX_E_STATE, "peer buffers are already open");
     if (!h->coop) return h->fail(VX_E_STATE, "the device has no cooperative launch");
     CK(cudaSetDevice(h->dev));
@@ -2096,7 +2103,7 @@ int vx_tp_p2p_open(vx_handle* h, const uint8_t* handles) {
     h->p2p_peer[r] = ptr;
   }
   h->p2p_ready = true;
-  h->use_mk = h->coop;
+  h->use_mk = h->coop && h->tp <= kMkMaxTp;
   return VX_OK;
 }
 
